@@ -1,0 +1,482 @@
+"""Benchmark of the sm_100a paged prefill attention (and the RoPE + KV-cache write).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--splits S]
+    python bench.py --impl reference ...   # the CPU implementation of the path, timed on host cores
+
+Default workload: chunked prefill at 16K context -- 64 sequences, 2048-token
+query chunks, total KV length uniform in [8192, 16384], 16 query heads / 2 KV
+heads, head_dim 128, bf16, page size 16, permuted block table.  Under
+torchrun the sequences are sharded contiguously over the ranks (one process
+per GPU, no collective in the timed region); the reported value is the
+causal FLOPs of all ranks divided by the slowest rank's device time.
+
+One JSON line on rank 0.  ``value``: device-resident throughput (inputs in HBM
+before the timed region).  ``e2e``: the same metric through the public
+operator API (``iluvatar_attention``) with the inputs copied from pinned host
+memory and the output copied back inside the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "minicpm-attention-optimization-iluvatar_b200"
+for _p in (str(ROOT), str(PKG_DIR)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "paged prefill attention TFLOP/s & tokens/s at 4K/16K ctx, 64 seqs, 1/2/4/8 B200; % TC peak"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="chunked_prefill_16k",
+                    choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "rope_16384"])
+    ap.add_argument("--splits", type=int, default=0, help="0 = automatic")
+    ap.add_argument("--rotary-dim", type=int, default=128)
+    ap.add_argument("--interleaved", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--verify", action="store_true", help="gather outputs to rank 0 (NCCL) and check sampled rows")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------- ranks
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------- peaks / clocks
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]) if parts[3] not in ("[N/A]", "") else None,
+                                 active=parts[4], hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        loaded = [r for r in rows if r["power"] is None or r["power"] > 200] or rows
+        reasons = set()
+        for r in loaded:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"), ("swt", "sw_thermal_slowdown"),
+                              ("pcap", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+# --------------------------------------------------------------------- workloads
+def shard(n: int, world: int, rank: int) -> list[int]:
+    from minicpm_b200.sharding import contiguous_shard
+
+    return contiguous_shard(n, world, rank)
+
+
+def build_local_batch(workload: str, world: int, rank: int):
+    from minicpm_b200 import workloads
+    from minicpm_b200.sharding import lpt_shard
+
+    q, kv = workloads.WORKLOADS[workload]()
+    if workload == "mixed_256":
+        ids = lpt_shard(q, kv, world, 16, 128)[rank]
+    else:
+        ids = shard(len(q), world, rank)
+    batch = workloads.build_attention_batch([q[i] for i in ids], [kv[i] for i in ids], seq_ids=ids)
+    return batch, q, kv
+
+
+def cpu_sample_flops(batch, rows: int):
+    """Oracle over the last ``rows`` query rows of the batch's first sequence."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import causal_flops, paged_attention_reference
+
+    from minicpm_b200.workloads import AttentionBatch
+
+    q_len, L = batch.query_lens[0], batch.kv_lens[0]
+    r1, r0 = q_len, max(0, q_len - rows)
+    sub = AttentionBatch(q=batch.q[r0:r1], kv_cache=batch.kv_cache, block_table=batch.block_table[:1],
+                         cu_seqlens_q=torch.tensor([0, r1 - r0], dtype=torch.int32),
+                         seqused_k=torch.tensor([L], dtype=torch.int32), query_lens=[r1 - r0], kv_lens=[L],
+                         softmax_scale=batch.softmax_scale, seq_ids=batch.seq_ids[:1])
+    flops = causal_flops([r1 - r0], [L], 16, 128)
+
+    def run():
+        paged_attention_reference(sub.q, sub.k_cache, sub.v_cache, sub.block_table, sub.cu_seqlens_q, sub.seqused_k,
+                                  sub.softmax_scale, q_chunk=256)
+
+    desc = f"oracle fp32 over query rows [{r0},{r1}) of sequence {batch.seq_ids[0]} (KV length {L})"
+    return run, flops, desc
+
+
+def time_cpu(run, reps: int):
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+# --------------------------------------------------------------------- reference arm
+def reference_arm(args, world, rank):
+    """The CPU implementation of the path (the fp32 oracle port), timed on host cores."""
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    if args.workload == "rope_16384":
+        print(json.dumps({"impl": "reference", "unavailable": "reference arm covers the attention workloads"}))
+        return
+    from minicpm_b200 import workloads
+
+    q, kv = workloads.WORKLOADS[args.workload]()
+    batch = workloads.build_attention_batch(q[:1], kv[:1], seq_ids=[0])
+    run, flops, desc = cpu_sample_flops(batch, 512)
+    for _ in range(args.warmup):
+        run()
+    times = time_cpu(run, args.steps)
+    total = sum(times)
+    value = flops * args.steps / total / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "sample": desc},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- RoPE bench
+def rope_bench(args, world, rank, local):
+    from minicpm_b200 import fused_rope_and_cache
+    from minicpm_b200.workloads import build_rope_batch, rope_algorithmic_bytes
+
+    b = build_rope_batch(16384, rotary_dim=args.rotary_dim, is_neox=not args.interleaved)
+    g = b.to(torch.device("cuda", local))
+    nbytes = rope_algorithmic_bytes(b)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def step():
+        fused_rope_and_cache(g.query, g.key, g.value, g.positions, g.cos_sin_cache, g.is_neox, g.key_cache,
+                             g.value_cache, g.slot_mapping)
+
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()  # evict L2 between timed launches
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    ms = max_over_ranks(statistics.median(times), world)
+    peaks, kind = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "RoPE + paged KV-cache write GB/s", "value": gbs * world, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "rope_16384", "tokens": 16384, "rotary_dim": args.rotary_dim,
+                       "is_neox": not args.interleaved, "algorithmic_bytes": nbytes, "l2": "flushed between launches"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": kind},
+            "gpu_launches": args.steps,
+        }), flush=True)
+
+
+# --------------------------------------------------------------------- attention bench
+def attention_bench(args, world, rank, local):
+    from minicpm_b200 import iluvatar_attention, paged_split_kv_attention
+    from minicpm_b200.split_kv_paged import choose_num_splits
+    from oracle import causal_flops  # FLOP formula of the reference harness (no compute)
+
+    dev = torch.device("cuda", local)
+    batch, all_q, all_kv = build_local_batch(args.workload, world, rank)
+    local_flops = causal_flops(batch.query_lens, batch.kv_lens, 16, 128)
+    total_flops = sum_over_ranks(float(local_flops), world) if world > 1 else float(local_flops)
+    total_tokens = sum(all_q)
+    g = batch.to(dev)
+    out = torch.empty_like(g.q)
+    splits = args.splits
+    resolved = splits or choose_num_splits(g.total_q, len(batch.query_lens), 16, 2, batch.max_seqlen_k)
+
+    def step():
+        paged_split_kv_attention(g.q, g.kv_cache[:, 0], g.kv_cache[:, 1], out, g.block_table, g.seqused_k,
+                                 g.cu_seqlens_q, g.max_seqlen_q, g.max_seqlen_k, g.softmax_scale, num_splits=splits)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    per_launch = []
+    with ClockSampler(dev.index) as clocks:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        start.record(stream)
+        for s, e in evs:
+            s.record(stream)
+            step()
+            e.record(stream)
+        end.record(stream)
+        end.synchronize()
+    barrier(world)
+    elapsed_ms = start.elapsed_time(end)
+    per_launch = [s.elapsed_time(e) for s, e in evs]
+    max_ms = max_over_ranks(elapsed_ms, world)
+    value = total_flops * args.steps / (max_ms * 1e-3) / 1e12
+    tokens_per_s = total_tokens * args.steps / (max_ms * 1e-3)
+
+    # e2e: public operator API, host buffers, copies inside the timed region.
+    e2e = None
+    if not args.no_e2e:
+        os.environ["ILUVATAR_USE_OPTIMIZED"] = "1"
+        os.environ["ILUVATAR_SPLIT_KV"] = "1"
+        if splits:
+            os.environ["ILUVATAR_NUM_SPLITS"] = str(splits)
+        host = {k: getattr(batch, k).pin_memory() for k in ("q", "kv_cache", "block_table", "cu_seqlens_q", "seqused_k")}
+        host_out = torch.empty(batch.q.shape, dtype=batch.q.dtype).pin_memory()
+        dq = torch.empty_like(g.q)
+        dkv = torch.empty_like(g.kv_cache)
+        dbt, dcu, dsu = torch.empty_like(g.block_table), torch.empty_like(g.cu_seqlens_q), torch.empty_like(g.seqused_k)
+        dout = torch.empty_like(g.q)
+        h2d = sum(t.numel() * t.element_size() for t in host.values())
+        d2h = host_out.numel() * host_out.element_size()
+
+        def e2e_step():
+            dq.copy_(host["q"], non_blocking=True)
+            dkv.copy_(host["kv_cache"], non_blocking=True)
+            dbt.copy_(host["block_table"], non_blocking=True)
+            dcu.copy_(host["cu_seqlens_q"], non_blocking=True)
+            dsu.copy_(host["seqused_k"], non_blocking=True)
+            iluvatar_attention(dq, dkv, dkv, dout, dcu, batch.max_seqlen_q, dsu, batch.max_seqlen_k,
+                               batch.softmax_scale, causal=True, block_table=dbt)
+            host_out.copy_(dout, non_blocking=True)
+
+        e2e_step()
+        barrier(world)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e.record(stream)
+        e.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(s.elapsed_time(e), world)
+        e2e = {"value": total_flops * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(sum_over_ranks(float(h2d), world)),
+               "d2h_bytes_per_step": int(sum_over_ranks(float(d2h), world)),
+               "ms_per_step": e2e_ms / args.steps,
+               "tokens_per_s": total_tokens * args.steps / (e2e_ms * 1e-3)}
+        assert torch.equal(host_out, out.cpu()), "e2e output differs from the device-resident run"
+
+    if args.verify:
+        from minicpm_b200.sharding import gather_rows_to_rank0
+
+        full = gather_rows_to_rank0(out, world, rank)
+        if rank == 0:
+            print(json.dumps({"verify_rows": int(full.shape[0])}), flush=True)
+
+    if rank != 0:
+        return
+    peaks, peak_kind = measured_peaks()
+    launch_ms = statistics.mean(per_launch)
+    achieved = local_flops / (launch_ms * 1e-3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / f"paged_attn_fwd_{args.workload}.traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            traffic = None
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        run, flops_s, desc = cpu_sample_flops(batch, 512)
+        run()
+        ts = time_cpu(run, 2)
+        cpu = {"value": flops_s / statistics.mean(ts) / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": desc}
+    l2_note = "inputs larger than L2 (KV %.0f MB + Q %.0f MB per GPU)" % (
+        g.kv_cache.numel() * 2 / 1e6 * (1 if world == 1 else 1), g.q.numel() * 2 / 1e6)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": max_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak" if args.workload == "mixed_256" else "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v, random-permuted page table)",
+        "tokens_per_s": tokens_per_s,
+        "tc_peak_frac": value / world / peaks["bf16_tflops"],
+        "config": {
+            "workload": args.workload,
+            "seqs": len(all_q),
+            "query_tokens": total_tokens,
+            "causal_flops": total_flops,
+            "heads": "16q/2kv", "head_dim": 128, "page_size": 16,
+            "num_splits": resolved,
+            "parallelism": f"sequence-sharded x{world}",
+            "l2": l2_note,
+        },
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
+                     "peak_kind": f"bf16_tflops (burst) of {peak_kind}",
+                     "per_launch_ms": launch_ms, "launch": "schedule + attention kernels of one call"},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "clocks": clocks.summary(),
+        "gpu_launches": args.steps * (2 + (1 if resolved > 1 else 0)),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        # Rank 0 alone times the host-core implementation; other ranks exit at once.
+        if int(os.environ.get("RANK", "0")) == 0:
+            reference_arm(args, int(os.environ.get("WORLD_SIZE", "1")), 0)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        if args.workload == "rope_16384":
+            rope_bench(args, world, rank, local)
+        else:
+            attention_bench(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,206 @@
+/*
+ * minicpm_b200.h -- C ABI of the sm_100a paged prefill attention and the
+ * fused RoPE + paged KV-cache write.
+ *
+ * Plain C: device pointers, element strides and sizes; no framework types.
+ * Every entry point returns a status code (B200_OK on success) and never
+ * throws; b200_last_error() gives the message of the last failure on the
+ * calling thread.  All work is enqueued on the given CUDA stream
+ * (a cudaStream_t passed as void*; NULL is the legacy default stream) and
+ * no entry point synchronises the host, allocates device memory or
+ * launches anything on another stream.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   b200_paged_attn_fwd    -> the two launches of paged_split_kv_attention,
+ *                             kernels/triton_split_kv_paged.py:283-360
+ *                             (_split_kv_forward :18-155, _split_kv_reduce
+ *                             :158-228), including the q-block compaction
+ *                             (:283-293) that the reference does on the host.
+ *   b200_split_combine     -> the _split_kv_reduce launch on its own,
+ *                             kernels/triton_split_kv_paged.py:342-360.
+ *   b200_rope_kv_write     -> the _rope_and_cache_kernel launch of
+ *                             fused_rope_and_cache,
+ *                             kernels/triton_rope_kv_cache.py:261-286.
+ *   b200_choose_num_splits -> the fixed split count of
+ *                             kernels/attention.py:166 and
+ *                             kernels/triton_unified_attention_optimized.py:216-218
+ *                             (the reference has no automatic choice).
+ *   b200_attn_workspace_bytes -> the per-call scratch allocation of
+ *                             kernels/triton_split_kv_paged.py:295-306.
+ */
+#ifndef MINICPM_B200_H_
+#define MINICPM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define B200_API __attribute__((visibility("default")))
+#else
+#define B200_API
+#endif
+
+/* Status codes. */
+#define B200_OK 0
+#define B200_ERR_INVALID 1     /* bad shape, stride, dtype or argument value  */
+#define B200_ERR_UNSUPPORTED 2 /* valid for the reference, not for this build */
+#define B200_ERR_CUDA 3        /* a CUDA runtime / driver call failed          */
+#define B200_ERR_WORKSPACE 4   /* workspace missing or too small               */
+
+/* Element types. */
+#define B200_DTYPE_F16 0
+#define B200_DTYPE_BF16 1
+#define B200_DTYPE_F32 2
+#define B200_DTYPE_I32 3
+#define B200_DTYPE_I64 4
+
+/* Device-side error codes (b200_device_error). */
+#define B200_DEVERR_NONE 0u
+#define B200_DEVERR_WAIT_TIMEOUT 1u /* an in-kernel wait ran past its limit     */
+#define B200_DEVERR_SLOT_RANGE 2u   /* slot_mapping entry >= num_blocks*bs      */
+#define B200_DEVERR_POS_RANGE 3u    /* position outside the cos/sin table        */
+
+/*
+ * Paged causal varlen attention (prefill / chunked prefill), GQA, Split-KV.
+ *
+ * q          [total_q, num_q_heads, head_dim], element strides q_stride_t/h, d contiguous
+ * k, v       paged caches [num_blocks, block_size, num_kv_heads, head_dim], strides
+ *            *_stride_block/_tok/_head, d contiguous (the cache[:, 0] / cache[:, 1]
+ *            views of a [num_blocks, 2, block_size, KH, D] cache are accepted)
+ * out        [total_q, num_q_heads, head_dim], written in place
+ * block_table [num_seqs, block_table_cols], int32 or int64, row stride in elements
+ * cu_seqlens_q [num_seqs + 1], seqused_k [num_seqs]: int32 or int64
+ * num_splits  0 = choose automatically, else 1..16
+ * workspace   device buffer of at least b200_attn_workspace_bytes(...) bytes,
+ *             owned by the caller; must not be shared by calls that overlap.
+ * All pointers: 16-byte aligned; all strides except d: multiples of 8 elements.
+ */
+typedef struct B200AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  const void* block_table;
+  const void* cu_seqlens_q;
+  const void* seqused_k;
+  int64_t q_stride_t, q_stride_h;
+  int64_t k_stride_block, k_stride_tok, k_stride_head;
+  int64_t v_stride_block, v_stride_tok, v_stride_head;
+  int64_t out_stride_t, out_stride_h;
+  int64_t block_table_stride;
+  int32_t block_table_cols;
+  int32_t block_table_dtype; /* B200_DTYPE_I32 / I64 */
+  int32_t seqlen_dtype;      /* dtype of cu_seqlens_q and seqused_k: I32 / I64 */
+  int32_t dtype;             /* q / k / v / out element type: F16 / BF16 */
+  int32_t num_seqs;
+  int32_t total_q;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t block_size;
+  int32_t num_blocks;
+  int32_t max_seqlen_q;
+  int32_t max_seqlen_k;
+  int32_t num_splits;
+  float softmax_scale;
+  void* workspace;
+  size_t workspace_bytes;
+} B200AttnParams;
+
+/* Workspace bytes b200_paged_attn_fwd needs for these sizes (num_splits 0 = auto). */
+B200_API size_t b200_attn_workspace_bytes(int32_t total_q, int32_t num_seqs, int32_t num_q_heads,
+                                 int32_t num_kv_heads, int32_t head_dim, int32_t num_splits,
+                                 int32_t max_seqlen_k, int32_t dtype);
+
+/* The split count b200_paged_attn_fwd uses for num_splits = 0. */
+B200_API int32_t b200_choose_num_splits(int32_t total_q, int32_t num_seqs, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t max_seqlen_k);
+
+B200_API int b200_paged_attn_fwd(const B200AttnParams* params, void* stream);
+
+/*
+ * Cross-split combine: out[t,h,:] = sum_s w_s O_s[t,h,:] / max(sum_s w_s, 1e-20),
+ * w_s = exp(m_s - max_s m_s) * l_s for l_s > 0, else 0.
+ * o_splits [num_splits, total_q, num_heads, head_dim] (F16 / BF16 / F32), m, l
+ * [num_splits, total_q, num_heads] F32, out [total_q, num_heads, head_dim]
+ * (F16 / BF16 / F32); d contiguous everywhere.
+ */
+typedef struct B200CombineParams {
+  const void* o_splits;
+  const float* m_splits;
+  const float* l_splits;
+  void* out;
+  int64_t o_stride_s, o_stride_t, o_stride_h;
+  int64_t m_stride_s, m_stride_t, m_stride_h;
+  int64_t l_stride_s, l_stride_t, l_stride_h;
+  int64_t out_stride_t, out_stride_h;
+  int32_t o_dtype;
+  int32_t out_dtype;
+  int32_t num_splits;
+  int32_t total_q;
+  int32_t num_heads;
+  int32_t head_dim;
+} B200CombineParams;
+
+B200_API int b200_split_combine(const B200CombineParams* params, void* stream);
+
+/*
+ * Fused RoPE + paged KV-cache write.  query [T, Hq, D] rotated in place;
+ * rotate(key) -> key_cache[slot / bs, slot % bs, h, :]; value -> value_cache[...];
+ * tokens with slot < 0 skip both cache writes.  cos_sin_cache [max_position,
+ * rotary_dim] = [cos(0..rd/2) | sin(0..rd/2)].  Caches [num_blocks, bs, Hkv, D].
+ */
+typedef struct B200RopeParams {
+  void* query;
+  const void* key;
+  const void* value;
+  const void* positions;
+  const void* cos_sin_cache;
+  void* key_cache;
+  void* value_cache;
+  const void* slot_mapping;
+  int64_t q_stride_t, q_stride_h, q_stride_d;
+  int64_t k_stride_t, k_stride_h, k_stride_d;
+  int64_t v_stride_t, v_stride_h, v_stride_d;
+  int64_t cos_sin_stride_t;
+  int64_t cache_stride_block, cache_stride_tok, cache_stride_head, cache_stride_d;
+  int32_t num_tokens;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t rotary_dim;
+  int32_t block_size;
+  int32_t num_blocks;
+  int32_t max_position;
+  int32_t is_neox;
+  int32_t dtype;          /* query / key / value / caches: F16 / BF16 */
+  int32_t cos_sin_dtype;  /* F16 / BF16 / F32 */
+  int32_t position_dtype; /* I32 / I64 */
+  int32_t slot_dtype;     /* I32 / I64 */
+} B200RopeParams;
+
+B200_API int b200_rope_kv_write(const B200RopeParams* params, void* stream);
+
+/* Message of the last failed call on this host thread ("" if none). */
+B200_API const char* b200_last_error(void);
+
+/*
+ * Synchronises `stream`, then reads and clears this library's device error
+ * word on the current device (B200_DEVERR_*).  For tests and debugging; the
+ * hot-path calls never synchronise.
+ */
+B200_API int b200_device_error(void* stream, uint32_t* code);
+
+B200_API int b200_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINICPM_B200_H_ */

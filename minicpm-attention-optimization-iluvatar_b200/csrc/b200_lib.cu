@@ -1,0 +1,422 @@
+// b200_lib.cu -- the C ABI declared in include/minicpm_b200.h.
+//
+// One translation unit: the kernels live in the headers included below.
+// Host code validates arguments (mirroring the reference's ValueError checks
+// in kernels/triton_split_kv_paged.py:249-281 and
+// kernels/triton_rope_kv_cache.py:219-260 where they apply to raw pointers),
+// encodes the TMA tensor maps, and enqueues the launches on the caller's
+// stream.  Nothing here synchronises, allocates, or falls back to another
+// implementation.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "minicpm_b200.h"
+#include "paged_attention.cuh"
+#include "rope_kv_cache.cuh"
+#include "split_combine.cuh"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return B200_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kNumSmsB200 = 148;
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kNumSmsB200;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return kNumSmsB200;
+  return n;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_map(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank, const void* base, const cuuint64_t* dims,
+               const cuuint64_t* strides_bytes, const cuuint32_t* box, const char* what) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  const CUresult r = enc(map, dt, rank, const_cast<void*>(base), dims, strides_bytes, box, elem_strides,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200_ERR_INVALID, "tensor map for %s rejected by the driver (CUresult %d)", what, (int)r);
+  return B200_OK;
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WorkspaceLayout {
+  size_t count_off, tile_base_off, units_off, o_off, m_off, l_off, total;
+  int capacity;
+};
+
+WorkspaceLayout attn_workspace_layout(int64_t total_q, int num_seqs, int hq, int hkv, int head_dim, int splits,
+                                      int elt) {
+  WorkspaceLayout w{};
+  const int group = hkv > 0 ? hq / hkv : 1;
+  const int ppt = group > 0 ? b200::kAttnTileM / group : 1;
+  const int64_t tiles_ub = (total_q + ppt - 1) / (ppt > 0 ? ppt : 1) + num_seqs;
+  const int64_t cap = tiles_ub * hkv * splits;
+  w.capacity = static_cast<int>(cap > 0x7fffffff ? 0x7fffffff : cap);
+  w.count_off = 0;
+  w.tile_base_off = 256;
+  w.units_off = align_up(w.tile_base_off + sizeof(int) * (num_seqs + 1), 256);
+  w.o_off = align_up(w.units_off + sizeof(int4) * static_cast<size_t>(w.capacity), 256);
+  w.m_off = w.o_off;
+  w.l_off = w.o_off;
+  w.total = w.o_off;
+  if (splits > 1) {
+    const size_t rows = static_cast<size_t>(splits) * total_q * hq;
+    w.m_off = align_up(w.o_off + rows * head_dim * elt, 256);
+    w.l_off = align_up(w.m_off + rows * sizeof(float), 256);
+    w.total = align_up(w.l_off + rows * sizeof(float), 256);
+  }
+  return w;
+}
+
+int auto_splits(int32_t total_q, int32_t num_seqs, int32_t hq, int32_t hkv, int32_t max_seqlen_k, int num_sms) {
+  if (hkv <= 0 || hq <= 0 || hq % hkv) return 1;
+  const int group = hq / hkv;
+  const int ppt = group <= b200::kAttnTileM ? b200::kAttnTileM / group : 1;
+  const int64_t units = ((int64_t)total_q + ppt - 1) / ppt * hkv;
+  int s = 1;
+  // Split the KV axis only while the grid is under one wave of CTAs and each
+  // split keeps at least two KV tiles of work.
+  while (s < b200::kMaxSplits && units * s < num_sms && (int64_t)max_seqlen_k >= (int64_t)s * 2 * 2 * b200::kAttnTileN)
+    s *= 2;
+  (void)num_seqs;
+  return s;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b200_abi_version(void) { return B200_ABI_VERSION; }
+
+const char* b200_last_error(void) { return g_last_error; }
+
+int32_t b200_choose_num_splits(int32_t total_q, int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                               int32_t max_seqlen_k) {
+  return auto_splits(total_q, num_seqs, num_q_heads, num_kv_heads, max_seqlen_k, sm_count());
+}
+
+size_t b200_attn_workspace_bytes(int32_t total_q, int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                                 int32_t head_dim, int32_t num_splits, int32_t max_seqlen_k, int32_t dtype) {
+  if (num_splits <= 0) num_splits = b200_choose_num_splits(total_q, num_seqs, num_q_heads, num_kv_heads, max_seqlen_k);
+  const int elt = (dtype == B200_DTYPE_F32) ? 4 : 2;
+  return attn_workspace_layout(total_q, num_seqs, num_q_heads, num_kv_heads, head_dim, num_splits, elt).total;
+}
+
+int b200_split_combine(const B200CombineParams* p, void* stream) {
+  if (!p) return fail(B200_ERR_INVALID, "null params");
+  if (p->num_splits < 1 || p->num_splits > b200::kMaxSplits)
+    return fail(B200_ERR_INVALID, "num_splits must be in [1, %d]", b200::kMaxSplits);
+  if (p->total_q < 0 || p->num_heads <= 0) return fail(B200_ERR_INVALID, "bad sizes");
+  if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256)
+    return fail(B200_ERR_INVALID, "head_dim must be 64, 128 or 256");
+  if (p->total_q == 0) return B200_OK;
+  const int oe = p->o_dtype == B200_DTYPE_F32 ? 4 : 2, ue = p->out_dtype == B200_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(p->o_splits) || !aligned16(p->out) || ((p->o_stride_s * oe) | (p->o_stride_t * oe) | (p->o_stride_h * oe)) & 15 ||
+      ((p->out_stride_t * ue) | (p->out_stride_h * ue)) & 15)
+    return fail(B200_ERR_UNSUPPORTED, "split combine needs 16-byte aligned rows of O and out");
+  b200::CombineArgs a{};
+  a.o = p->o_splits; a.m = p->m_splits; a.l = p->l_splits; a.out = p->out;
+  a.o_ss = p->o_stride_s; a.o_st = p->o_stride_t; a.o_sh = p->o_stride_h;
+  a.m_ss = p->m_stride_s; a.m_st = p->m_stride_t; a.m_sh = p->m_stride_h;
+  a.l_ss = p->l_stride_s; a.l_st = p->l_stride_t; a.l_sh = p->l_stride_h;
+  a.out_st = p->out_stride_t; a.out_sh = p->out_stride_h;
+  a.num_splits = p->num_splits; a.total_q = p->total_q; a.num_heads = p->num_heads;
+  const int64_t rows = (int64_t)p->total_q * p->num_heads;
+  const int rows_per_block = b200::kCombineThreads / (p->head_dim / 8);
+  const dim3 grid((unsigned)((rows + rows_per_block - 1) / rows_per_block));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+#define B200_COMBINE_D(TO, TOUT)                                                                   \
+  switch (p->head_dim) {                                                                          \
+    case 64: b200::split_combine_kernel<TO, TOUT, 64><<<grid, b200::kCombineThreads, 0, s>>>(a); break;   \
+    case 128: b200::split_combine_kernel<TO, TOUT, 128><<<grid, b200::kCombineThreads, 0, s>>>(a); break; \
+    default: b200::split_combine_kernel<TO, TOUT, 256><<<grid, b200::kCombineThreads, 0, s>>>(a); break;  \
+  }
+#define B200_COMBINE_OUT(TO)                                                            \
+  switch (p->out_dtype) {                                                               \
+    case B200_DTYPE_BF16: B200_COMBINE_D(TO, __nv_bfloat16) break;                      \
+    case B200_DTYPE_F16: B200_COMBINE_D(TO, __half) break;                              \
+    case B200_DTYPE_F32: B200_COMBINE_D(TO, float) break;                               \
+    default: return fail(B200_ERR_INVALID, "out dtype must be f16, bf16 or f32");       \
+  }
+  switch (p->o_dtype) {
+    case B200_DTYPE_BF16: B200_COMBINE_OUT(__nv_bfloat16) break;
+    case B200_DTYPE_F16: B200_COMBINE_OUT(__half) break;
+    case B200_DTYPE_F32: B200_COMBINE_OUT(float) break;
+    default: return fail(B200_ERR_INVALID, "o_splits dtype must be f16, bf16 or f32");
+  }
+#undef B200_COMBINE_OUT
+#undef B200_COMBINE_D
+  return check_launch("split_combine_kernel");
+}
+
+int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
+  if (!p) return fail(B200_ERR_INVALID, "null params");
+  if (p->dtype != B200_DTYPE_BF16 && p->dtype != B200_DTYPE_F16)
+    return fail(B200_ERR_UNSUPPORTED, "q/k/v/out must be bf16 or f16 for the sm_100a kernel");
+  if (p->num_q_heads <= 0 || p->num_kv_heads <= 0 || p->num_q_heads % p->num_kv_heads)
+    return fail(B200_ERR_INVALID, "unsupported head shape for paged Split-KV");
+  if (p->block_size <= 0 || p->block_size % 16) return fail(B200_ERR_INVALID, "unsupported head shape for paged Split-KV");
+  if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256)
+    return fail(B200_ERR_INVALID, "unsupported head shape for paged Split-KV");
+  if (p->head_dim != b200::kAttnHeadDim)
+    return fail(B200_ERR_UNSUPPORTED, "head_dim %d: the sm_100a kernel is built for head_dim 128", p->head_dim);
+  const int group = p->num_q_heads / p->num_kv_heads;
+  if (group > b200::kAttnTileM || b200::kAttnTileM % group)
+    return fail(B200_ERR_UNSUPPORTED, "query heads per KV head (%d) must divide 128", group);
+  if (p->num_splits < 0 || p->num_splits > b200::kMaxSplits)
+    return fail(B200_ERR_INVALID, "num_splits must be 0 (auto) or in [1, 16]");
+  if (p->num_seqs < 0 || p->total_q < 0 || p->num_blocks <= 0 || p->block_table_cols <= 0)
+    return fail(B200_ERR_INVALID, "bad sizes");
+  if (p->block_table_dtype != B200_DTYPE_I32 && p->block_table_dtype != B200_DTYPE_I64)
+    return fail(B200_ERR_INVALID, "block_table must contain integer physical block ids");
+  if (p->seqlen_dtype != B200_DTYPE_I32 && p->seqlen_dtype != B200_DTYPE_I64)
+    return fail(B200_ERR_INVALID, "cu_seqlens_q and seqused_k must be int32 or int64");
+  if (p->total_q == 0 || p->num_seqs == 0) return B200_OK;
+  const int elt = 2;
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->out))
+    return fail(B200_ERR_UNSUPPORTED, "q, k, v and out must be 16-byte aligned");
+  if (((p->q_stride_t | p->q_stride_h | p->k_stride_block | p->k_stride_tok | p->k_stride_head | p->v_stride_block |
+        p->v_stride_tok | p->v_stride_head | p->out_stride_t | p->out_stride_h) *
+       elt) & 15)
+    return fail(B200_ERR_UNSUPPORTED, "token/head/block strides must be multiples of 16 bytes");
+
+  const int splits = p->num_splits > 0 ? p->num_splits
+                                       : b200_choose_num_splits(p->total_q, p->num_seqs, p->num_q_heads,
+                                                                p->num_kv_heads, p->max_seqlen_k);
+  const WorkspaceLayout w =
+      attn_workspace_layout(p->total_q, p->num_seqs, p->num_q_heads, p->num_kv_heads, p->head_dim, splits, elt);
+  if (!p->workspace || p->workspace_bytes < w.total)
+    return fail(B200_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", w.total, p->workspace_bytes);
+  if (!aligned16(p->workspace)) return fail(B200_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(p->workspace);
+
+  const CUtensorMapDataType dt = p->dtype == B200_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int ppt = b200::kAttnTileM / group;
+  CUtensorMap tm_q, tm_k, tm_v;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)p->head_dim, (cuuint64_t)p->num_q_heads, (cuuint64_t)p->total_q};
+    const cuuint64_t strides[2] = {(cuuint64_t)(p->q_stride_h * elt), (cuuint64_t)(p->q_stride_t * elt)};
+    const cuuint32_t box[3] = {64, (cuuint32_t)group, (cuuint32_t)ppt};
+    if (int r = encode_map(&tm_q, dt, 3, p->q, dims, strides, box, "q")) return r;
+  }
+  {
+    const cuuint64_t dims[4] = {(cuuint64_t)p->head_dim, (cuuint64_t)p->block_size, (cuuint64_t)p->num_kv_heads,
+                                (cuuint64_t)p->num_blocks};
+    const cuuint32_t box[4] = {64, 16, 1, 1};
+    const cuuint64_t ks[3] = {(cuuint64_t)(p->k_stride_tok * elt), (cuuint64_t)(p->k_stride_head * elt),
+                              (cuuint64_t)(p->k_stride_block * elt)};
+    if (int r = encode_map(&tm_k, dt, 4, p->k, dims, ks, box, "k")) return r;
+    const cuuint64_t vs[3] = {(cuuint64_t)(p->v_stride_tok * elt), (cuuint64_t)(p->v_stride_head * elt),
+                              (cuuint64_t)(p->v_stride_block * elt)};
+    if (int r = encode_map(&tm_v, dt, 4, p->v, dims, vs, box, "v")) return r;
+  }
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  b200::SchedArgs sa{};
+  sa.cu_q = p->cu_seqlens_q;
+  sa.seqused = p->seqused_k;
+  sa.len_i64 = p->seqlen_dtype == B200_DTYPE_I64;
+  sa.num_seqs = p->num_seqs;
+  sa.pos_per_tile = ppt;
+  sa.num_kv_heads = p->num_kv_heads;
+  sa.num_splits = splits;
+  sa.capacity = w.capacity;
+  sa.tile_base = reinterpret_cast<int*>(ws + w.tile_base_off);
+  sa.units = reinterpret_cast<int4*>(ws + w.units_off);
+  sa.unit_count = reinterpret_cast<int*>(ws + w.count_off);
+  b200::attn_schedule_kernel<<<1, b200::kSchedThreads, 0, s>>>(sa);
+  if (int r = check_launch("attn_schedule_kernel")) return r;
+
+  b200::AttnKernelArgs a{};
+  a.block_table = p->block_table;
+  a.cu_q = p->cu_seqlens_q;
+  a.seqused = p->seqused_k;
+  a.out = p->out;
+  a.o_split = ws + w.o_off;
+  a.m_split = reinterpret_cast<float*>(ws + w.m_off);
+  a.l_split = reinterpret_cast<float*>(ws + w.l_off);
+  a.units = sa.units;
+  a.unit_count = sa.unit_count;
+  a.bt_stride = p->block_table_stride;
+  a.out_st = p->out_stride_t;
+  a.out_sh = p->out_stride_h;
+  a.bt_cols = p->block_table_cols;
+  a.bt_i64 = p->block_table_dtype == B200_DTYPE_I64;
+  a.len_i64 = sa.len_i64;
+  a.total_q = p->total_q;
+  a.num_q_heads = p->num_q_heads;
+  a.group = group;
+  a.pos_per_tile = ppt;
+  a.block_size = p->block_size;
+  a.num_blocks = p->num_blocks;
+  a.num_splits = splits;
+  a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
+
+  const dim3 grid(static_cast<unsigned>(w.capacity));
+  if (p->dtype == B200_DTYPE_BF16) {
+    auto k = b200::paged_attn_fwd_kernel<__nv_bfloat16>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kAttnSmemAlloc);
+    k<<<grid, b200::kAttnThreads, b200::kAttnSmemAlloc, s>>>(tm_q, tm_k, tm_v, a);
+  } else {
+    auto k = b200::paged_attn_fwd_kernel<__half>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kAttnSmemAlloc);
+    k<<<grid, b200::kAttnThreads, b200::kAttnSmemAlloc, s>>>(tm_q, tm_k, tm_v, a);
+  }
+  if (int r = check_launch("paged_attn_fwd_kernel")) return r;
+
+  if (splits > 1) {
+    B200CombineParams c{};
+    c.o_splits = ws + w.o_off;
+    c.m_splits = a.m_split;
+    c.l_splits = a.l_split;
+    c.out = p->out;
+    c.o_stride_h = p->head_dim;
+    c.o_stride_t = (int64_t)p->num_q_heads * p->head_dim;
+    c.o_stride_s = c.o_stride_t * p->total_q;
+    c.m_stride_h = c.l_stride_h = 1;
+    c.m_stride_t = c.l_stride_t = p->num_q_heads;
+    c.m_stride_s = c.l_stride_s = (int64_t)p->num_q_heads * p->total_q;
+    c.out_stride_t = p->out_stride_t;
+    c.out_stride_h = p->out_stride_h;
+    c.o_dtype = p->dtype;
+    c.out_dtype = p->dtype;
+    c.num_splits = splits;
+    c.total_q = p->total_q;
+    c.num_heads = p->num_q_heads;
+    c.head_dim = p->head_dim;
+    return b200_split_combine(&c, stream);
+  }
+  return B200_OK;
+}
+
+int b200_rope_kv_write(const B200RopeParams* p, void* stream) {
+  if (!p) return fail(B200_ERR_INVALID, "null params");
+  if (p->dtype != B200_DTYPE_BF16 && p->dtype != B200_DTYPE_F16)
+    return fail(B200_ERR_INVALID, "only unquantized BF16/FP16 caches are supported");
+  if (p->position_dtype != B200_DTYPE_I32 && p->position_dtype != B200_DTYPE_I64)
+    return fail(B200_ERR_INVALID, "positions and slot_mapping must contain integer indices");
+  if (p->slot_dtype != B200_DTYPE_I32 && p->slot_dtype != B200_DTYPE_I64)
+    return fail(B200_ERR_INVALID, "positions and slot_mapping must contain integer indices");
+  if (p->cos_sin_dtype != B200_DTYPE_BF16 && p->cos_sin_dtype != B200_DTYPE_F16 && p->cos_sin_dtype != B200_DTYPE_F32)
+    return fail(B200_ERR_INVALID, "cos_sin_cache must be f16, bf16 or f32");
+  if (p->rotary_dim <= 0 || p->rotary_dim > p->head_dim || p->rotary_dim % 2 || p->num_q_heads < p->num_kv_heads ||
+      (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256) || p->block_size <= 0 || p->block_size % 16 ||
+      p->num_kv_heads <= 0)
+    return fail(B200_ERR_INVALID, "unsupported RoPE/cache shape");
+  if (p->num_tokens <= 0) return B200_OK;
+
+  b200::RopeArgs a{};
+  a.q = p->query; a.k = p->key; a.v = p->value; a.pos = p->positions; a.cs = p->cos_sin_cache;
+  a.kc = p->key_cache; a.vc = p->value_cache; a.slot = p->slot_mapping;
+  a.q_st = p->q_stride_t; a.q_sh = p->q_stride_h; a.q_sd = p->q_stride_d;
+  a.k_st = p->k_stride_t; a.k_sh = p->k_stride_h; a.k_sd = p->k_stride_d;
+  a.v_st = p->v_stride_t; a.v_sh = p->v_stride_h; a.v_sd = p->v_stride_d;
+  a.cs_st = p->cos_sin_stride_t;
+  a.c_sb = p->cache_stride_block; a.c_st = p->cache_stride_tok; a.c_sh = p->cache_stride_head; a.c_sd = p->cache_stride_d;
+  a.num_slots = (int64_t)p->num_blocks * p->block_size;
+  a.num_tokens = p->num_tokens; a.hq = p->num_q_heads; a.hkv = p->num_kv_heads; a.head_dim = p->head_dim;
+  a.rd = p->rotary_dim; a.block_size = p->block_size; a.max_position = p->max_position;
+  a.pos_i64 = p->position_dtype == B200_DTYPE_I64;
+  a.slot_i64 = p->slot_dtype == B200_DTYPE_I64;
+
+  const int cse = p->cos_sin_dtype == B200_DTYPE_F32 ? 4 : 2;
+  const bool vec_ok = p->q_stride_d == 1 && p->k_stride_d == 1 && p->v_stride_d == 1 && p->cache_stride_d == 1 &&
+                      aligned16(p->query) && aligned16(p->key) && aligned16(p->value) && aligned16(p->key_cache) &&
+                      aligned16(p->value_cache) && aligned16(p->cos_sin_cache) &&
+                      (((p->q_stride_t | p->q_stride_h | p->k_stride_t | p->k_stride_h | p->v_stride_t | p->v_stride_h |
+                         p->cache_stride_block | p->cache_stride_tok | p->cache_stride_head) * 2) & 15) == 0 &&
+                      ((p->cos_sin_stride_t * cse) & 15) == 0 &&
+                      (p->is_neox ? (p->rotary_dim % 16 == 0) : (p->rotary_dim % 8 == 0));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec_ok) {
+    const int half = p->rotary_dim / 2;
+    const int n_rot = p->is_neox ? half / 8 : p->rotary_dim / 8;
+    const int per_token = p->num_q_heads * n_rot + p->num_kv_heads * (n_rot + (p->head_dim - p->rotary_dim) / 8) +
+                          p->num_kv_heads * (p->head_dim / 8);
+    const int64_t threads = (int64_t)per_token * p->num_tokens;
+    const dim3 grid((unsigned)((threads + b200::kRopeThreads - 1) / b200::kRopeThreads));
+#define B200_ROPE_VEC(T, CS)                                                                                     \
+  if (p->is_neox) b200::rope_kv_vec_kernel<T, CS, true><<<grid, b200::kRopeThreads, 0, s>>>(a);                   \
+  else b200::rope_kv_vec_kernel<T, CS, false><<<grid, b200::kRopeThreads, 0, s>>>(a);
+#define B200_ROPE_CS(T)                                                         \
+  switch (p->cos_sin_dtype) {                                                   \
+    case B200_DTYPE_BF16: B200_ROPE_VEC(T, __nv_bfloat16) break;                \
+    case B200_DTYPE_F16: B200_ROPE_VEC(T, __half) break;                        \
+    default: B200_ROPE_VEC(T, float) break;                                     \
+  }
+    if (p->dtype == B200_DTYPE_BF16) { B200_ROPE_CS(__nv_bfloat16) } else { B200_ROPE_CS(__half) }
+#undef B200_ROPE_CS
+#undef B200_ROPE_VEC
+    return check_launch("rope_kv_vec_kernel");
+  }
+  const int half = p->rotary_dim / 2;
+  const int per_token = p->num_q_heads * half + p->num_kv_heads * (half + (p->head_dim - p->rotary_dim)) +
+                        p->num_kv_heads * p->head_dim;
+  const int64_t threads = (int64_t)per_token * p->num_tokens;
+  const dim3 grid((unsigned)((threads + b200::kRopeThreads - 1) / b200::kRopeThreads));
+#define B200_ROPE_SC(T, CS) b200::rope_kv_scalar_kernel<T, CS><<<grid, b200::kRopeThreads, 0, s>>>(a, p->is_neox);
+#define B200_ROPE_SCS(T)                                                 \
+  switch (p->cos_sin_dtype) {                                            \
+    case B200_DTYPE_BF16: B200_ROPE_SC(T, __nv_bfloat16) break;          \
+    case B200_DTYPE_F16: B200_ROPE_SC(T, __half) break;                  \
+    default: B200_ROPE_SC(T, float) break;                               \
+  }
+  if (p->dtype == B200_DTYPE_BF16) { B200_ROPE_SCS(__nv_bfloat16) } else { B200_ROPE_SCS(__half) }
+#undef B200_ROPE_SCS
+#undef B200_ROPE_SC
+  return check_launch("rope_kv_scalar_kernel");
+}
+
+int b200_device_error(void* stream, uint32_t* code) {
+  if (!code) return fail(B200_ERR_INVALID, "null code pointer");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "stream synchronize: %s", cudaGetErrorString(e));
+  unsigned int v = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&v, b200::g_device_error, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(b200::g_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "device error word: %s", cudaGetErrorString(e));
+  *code = v;
+  return B200_OK;
+}
+
+}  // extern "C"

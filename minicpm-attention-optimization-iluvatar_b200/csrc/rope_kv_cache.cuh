@@ -1,0 +1,255 @@
+// rope_kv_cache.cuh -- fused RoPE + paged KV-cache write.
+//
+// Semantics of _rope_and_cache_kernel (kernels/triton_rope_kv_cache.py:49-202
+// of the reference project):
+//   * cos_sin_cache[pos] = [cos(0..rd/2) | sin(0..rd/2)];
+//   * NeoX pairs (d, d + rd/2), interleaved pairs (2i, 2i + 1);
+//     first' = x1*cos - x2*sin, second' = x2*cos + x1*sin, in fp32, each
+//     product rounded before the add (no fused multiply-add), then rounded
+//     to the storage dtype (round to nearest even);
+//   * dims >= rotary_dim pass through;
+//   * Q is rotated in place for every token; rotated K and unchanged V go to
+//     cache[slot / bs, slot % bs, h, :] unless slot < 0.
+// Out-of-range indices, which the reference would read or write out of
+// bounds, are skipped here and recorded in the device error word.
+//
+// Bandwidth kernel: one thread per 8-element unit (a NeoX unit is the chunk
+// at d plus its partner chunk at d + rd/2), 16-byte loads and stores.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "split_combine.cuh"
+
+namespace b200 {
+
+constexpr int kRopeThreads = 256;
+
+struct RopeArgs {
+  void* q;
+  const void* k;
+  const void* v;
+  const void* pos;
+  const void* cs;
+  void* kc;
+  void* vc;
+  const void* slot;
+  int64_t q_st, q_sh, q_sd;
+  int64_t k_st, k_sh, k_sd;
+  int64_t v_st, v_sh, v_sd;
+  int64_t cs_st;
+  int64_t c_sb, c_st, c_sh, c_sd;
+  int64_t num_slots;
+  int num_tokens, hq, hkv, head_dim, rd, block_size, max_position;
+  int pos_i64, slot_i64;
+};
+
+__device__ __forceinline__ int64_t load_i(const void* p, int64_t i, int is_i64) {
+  return is_i64 ? static_cast<const int64_t*>(p)[i] : static_cast<int64_t>(static_cast<const int*>(p)[i]);
+}
+
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&v)[4]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+template <>
+__device__ __forceinline__ void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 a = *reinterpret_cast<const uint2*>(p);
+  const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.x));
+  const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.y));
+  v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+}
+template <>
+__device__ __forceinline__ void load4<__half>(const __half* p, float (&v)[4]) {
+  const uint2 a = *reinterpret_cast<const uint2*>(p);
+  const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&a.x));
+  const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&a.y));
+  v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// first' = a*c - b*s ; second' = b*c + a*s, products rounded separately.
+__device__ __forceinline__ void rotate_pair(float a, float b, float c, float s, float& ra, float& rb) {
+  ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  rb = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+
+// Vector path: d contiguous and 16-byte aligned rows; rd % 16 == 0 (NeoX) or rd % 8 == 0.
+template <typename T, typename CS, bool NEOX>
+__global__ void __launch_bounds__(kRopeThreads) rope_kv_vec_kernel(const RopeArgs a) {
+  const int half = a.rd / 2;
+  const int n_rot = NEOX ? half / 8 : a.rd / 8;  // rotation units per head
+  const int n_pass = (a.head_dim - a.rd) / 8;     // K pass-through chunks per head
+  const int n_v = a.head_dim / 8;                 // V chunks per head
+  const int q_items = a.hq * n_rot;
+  const int k_items = a.hkv * (n_rot + n_pass);
+  const int per_token = q_items + k_items + a.hkv * n_v;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t token = gid / per_token;
+  if (token >= a.num_tokens) return;
+  int item = static_cast<int>(gid - token * per_token);
+
+  const int64_t pos = load_i(a.pos, token, a.pos_i64);
+  if (pos < 0 || pos >= a.max_position) {
+    if (item == 0) record_device_error(B200_DEVERR_POS_RANGE);
+    return;
+  }
+  const CS* cs_row = static_cast<const CS*>(a.cs) + pos * a.cs_st;
+
+  if (item < q_items) {
+    const int h = item / n_rot, u = item - h * n_rot;
+    T* qrow = static_cast<T*>(a.q) + token * a.q_st + h * a.q_sh;
+    if (NEOX) {
+      float x1[8], x2[8], c[8], s[8];
+      load8<T>(qrow + 8 * u, x1);
+      load8<T>(qrow + half + 8 * u, x2);
+      load8<CS>(cs_row + 8 * u, c);
+      load8<CS>(cs_row + half + 8 * u, s);
+      float y1[8], y2[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rotate_pair(x1[i], x2[i], c[i], s[i], y1[i], y2[i]);
+      store8<T>(qrow + 8 * u, y1);
+      store8<T>(qrow + half + 8 * u, y2);
+    } else {
+      float x[8], c[4], s[4], y[8];
+      load8<T>(qrow + 8 * u, x);
+      load4<CS>(cs_row + 4 * u, c);
+      load4<CS>(cs_row + half + 4 * u, s);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rotate_pair(x[2 * i], x[2 * i + 1], c[i], s[i], y[2 * i], y[2 * i + 1]);
+      store8<T>(qrow + 8 * u, y);
+    }
+    return;
+  }
+  item -= q_items;
+
+  const int64_t slot = load_i(a.slot, token, a.slot_i64);
+  if (slot < 0) return;
+  if (slot >= a.num_slots) {
+    if (item == 0) record_device_error(B200_DEVERR_SLOT_RANGE);
+    return;
+  }
+  const int64_t blk = slot / a.block_size, off = slot - blk * a.block_size;
+
+  if (item < k_items) {
+    const int per_head = n_rot + n_pass;
+    const int h = item / per_head, u = item - h * per_head;
+    const T* krow = static_cast<const T*>(a.k) + token * a.k_st + h * a.k_sh;
+    T* crow = static_cast<T*>(a.kc) + blk * a.c_sb + off * a.c_st + h * a.c_sh;
+    if (u >= n_rot) {  // pass-through chunk
+      const int d = a.rd + 8 * (u - n_rot);
+      *reinterpret_cast<uint4*>(crow + d) = *reinterpret_cast<const uint4*>(krow + d);
+      return;
+    }
+    if (NEOX) {
+      float x1[8], x2[8], c[8], s[8], y1[8], y2[8];
+      load8<T>(krow + 8 * u, x1);
+      load8<T>(krow + half + 8 * u, x2);
+      load8<CS>(cs_row + 8 * u, c);
+      load8<CS>(cs_row + half + 8 * u, s);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rotate_pair(x1[i], x2[i], c[i], s[i], y1[i], y2[i]);
+      store8<T>(crow + 8 * u, y1);
+      store8<T>(crow + half + 8 * u, y2);
+    } else {
+      float x[8], c[4], s[4], y[8];
+      load8<T>(krow + 8 * u, x);
+      load4<CS>(cs_row + 4 * u, c);
+      load4<CS>(cs_row + half + 4 * u, s);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rotate_pair(x[2 * i], x[2 * i + 1], c[i], s[i], y[2 * i], y[2 * i + 1]);
+      store8<T>(crow + 8 * u, y);
+    }
+    return;
+  }
+  item -= k_items;
+  const int h = item / n_v, u = item - h * n_v;
+  const T* vrow = static_cast<const T*>(a.v) + token * a.v_st + h * a.v_sh;
+  T* crow = static_cast<T*>(a.vc) + blk * a.c_sb + off * a.c_st + h * a.c_sh;
+  *reinterpret_cast<uint4*>(crow + 8 * u) = *reinterpret_cast<const uint4*>(vrow + 8 * u);
+}
+
+// Element path for any strides: one thread per rotation pair or copied element.
+template <typename T, typename CS>
+__global__ void __launch_bounds__(kRopeThreads) rope_kv_scalar_kernel(const RopeArgs a, const int neox) {
+  const int half = a.rd / 2;
+  const int q_items = a.hq * half;
+  const int k_items = a.hkv * (half + (a.head_dim - a.rd));
+  const int per_token = q_items + k_items + a.hkv * a.head_dim;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t token = gid / per_token;
+  if (token >= a.num_tokens) return;
+  int item = static_cast<int>(gid - token * per_token);
+  const int64_t pos = load_i(a.pos, token, a.pos_i64);
+  if (pos < 0 || pos >= a.max_position) {
+    if (item == 0) record_device_error(B200_DEVERR_POS_RANGE);
+    return;
+  }
+  const CS* cs_row = static_cast<const CS*>(a.cs) + pos * a.cs_st;
+  auto pair_dims = [&](int i, int& d1, int& d2) {
+    if (neox) { d1 = i; d2 = i + half; } else { d1 = 2 * i; d2 = 2 * i + 1; }
+  };
+  if (item < q_items) {
+    const int h = item / half, i = item - h * half;
+    int d1, d2;
+    pair_dims(i, d1, d2);
+    T* qrow = static_cast<T*>(a.q) + token * a.q_st + h * a.q_sh;
+    float y1, y2;
+    rotate_pair(to_f32(qrow[d1 * a.q_sd]), to_f32(qrow[d2 * a.q_sd]), to_f32(cs_row[i]), to_f32(cs_row[half + i]), y1, y2);
+    qrow[d1 * a.q_sd] = from_f32<T>(y1);
+    qrow[d2 * a.q_sd] = from_f32<T>(y2);
+    return;
+  }
+  item -= q_items;
+  const int64_t slot = load_i(a.slot, token, a.slot_i64);
+  if (slot < 0) return;
+  if (slot >= a.num_slots) {
+    if (item == 0) record_device_error(B200_DEVERR_SLOT_RANGE);
+    return;
+  }
+  const int64_t blk = slot / a.block_size, off = slot - blk * a.block_size;
+  if (item < k_items) {
+    const int per_head = half + (a.head_dim - a.rd);
+    const int h = item / per_head, u = item - h * per_head;
+    const T* krow = static_cast<const T*>(a.k) + token * a.k_st + h * a.k_sh;
+    T* crow = static_cast<T*>(a.kc) + blk * a.c_sb + off * a.c_st + h * a.c_sh;
+    if (u >= half) {
+      const int d = a.rd + (u - half);
+      crow[d * a.c_sd] = krow[d * a.k_sd];
+      return;
+    }
+    int d1, d2;
+    pair_dims(u, d1, d2);
+    float y1, y2;
+    rotate_pair(to_f32(krow[d1 * a.k_sd]), to_f32(krow[d2 * a.k_sd]), to_f32(cs_row[u]), to_f32(cs_row[half + u]), y1, y2);
+    crow[d1 * a.c_sd] = from_f32<T>(y1);
+    crow[d2 * a.c_sd] = from_f32<T>(y2);
+    return;
+  }
+  item -= k_items;
+  const int h = item / a.head_dim, d = item - h * a.head_dim;
+  const T* vrow = static_cast<const T*>(a.v) + token * a.v_st + h * a.v_sh;
+  T* crow = static_cast<T*>(a.vc) + blk * a.c_sb + off * a.c_st + h * a.c_sh;
+  crow[d * a.c_sd] = vrow[d * a.v_sd];
+}
+
+}  // namespace b200

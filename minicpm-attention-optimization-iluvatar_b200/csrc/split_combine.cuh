@@ -1,0 +1,140 @@
+// split_combine.cuh -- LSE-weighted combine of Split-KV partial outputs.
+//
+// Follows _split_kv_reduce (kernels/triton_split_kv_paged.py:197-228 of the
+// reference project): m* = max_s m_s; w_s = exp(m_s - m*) * l_s when l_s > 0,
+// else 0; out = sum_s w_s O_s / max(sum_s w_s, 1e-20).  A split with
+// l_s == 0 is never read (the reference multiplies it by 0).
+//
+// Bandwidth kernel: one (token, head) row per group of D/8 threads, each
+// thread moving 8 elements with 16-byte loads and stores.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sm100_ptx.cuh"
+
+namespace b200 {
+
+constexpr int kCombineThreads = 256;
+constexpr int kMaxSplits = 16;
+
+struct CombineArgs {
+  const void* o;
+  const float* m;
+  const float* l;
+  void* out;
+  int64_t o_ss, o_st, o_sh;
+  int64_t m_ss, m_st, m_sh;
+  int64_t l_ss, l_st, l_sh;
+  int64_t out_st, out_sh;
+  int num_splits, total_q, num_heads;
+};
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 w;
+  __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 c = __floats2bfloat162_rn(v[4], v[5]), d = __floats2bfloat162_rn(v[6], v[7]);
+  w.x = *reinterpret_cast<uint32_t*>(&a);
+  w.y = *reinterpret_cast<uint32_t*>(&b);
+  w.z = *reinterpret_cast<uint32_t*>(&c);
+  w.w = *reinterpret_cast<uint32_t*>(&d);
+  *reinterpret_cast<uint4*>(p) = w;
+}
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float (&v)[8]) {
+  uint4 w;
+  __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+  __half2 c = __floats2half2_rn(v[4], v[5]), d = __floats2half2_rn(v[6], v[7]);
+  w.x = *reinterpret_cast<uint32_t*>(&a);
+  w.y = *reinterpret_cast<uint32_t*>(&b);
+  w.z = *reinterpret_cast<uint32_t*>(&c);
+  w.w = *reinterpret_cast<uint32_t*>(&d);
+  *reinterpret_cast<uint4*>(p) = w;
+}
+
+template <typename TO, typename TOut, int D>
+__global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const CombineArgs a) {
+  constexpr int kThreadsPerRow = D / 8;
+  constexpr int kRowsPerBlock = kCombineThreads / kThreadsPerRow;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / kThreadsPerRow;
+  const int d0 = (threadIdx.x % kThreadsPerRow) * 8;
+  const int64_t nrows = static_cast<int64_t>(a.total_q) * a.num_heads;
+  if (row >= nrows) return;
+  const int64_t t = row / a.num_heads;
+  const int64_t h = row - t * a.num_heads;
+
+  float mv[kMaxSplits], lv[kMaxSplits];
+  float m_max = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < kMaxSplits; ++s) {
+    if (s < a.num_splits) {
+      mv[s] = a.m[s * a.m_ss + t * a.m_st + h * a.m_sh];
+      lv[s] = a.l[s * a.l_ss + t * a.l_st + h * a.l_sh];
+      m_max = fmaxf(m_max, mv[s]);
+    } else {
+      mv[s] = -INFINITY;
+      lv[s] = 0.f;
+    }
+  }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float denom = 0.f;
+  const TO* o = static_cast<const TO*>(a.o) + t * a.o_st + h * a.o_sh + d0;
+#pragma unroll
+  for (int s = 0; s < kMaxSplits; ++s) {
+    if (s < a.num_splits && lv[s] > 0.f) {
+      const float w = expf(mv[s] - m_max) * lv[s];
+      float v[8];
+      load8<TO>(o + s * a.o_ss, v);
+      denom += w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, v[i], acc[i]);
+    }
+  }
+  const float inv = 1.f / fmaxf(denom, 1e-20f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] *= inv;
+  store8<TOut>(static_cast<TOut*>(a.out) + t * a.out_st + h * a.out_sh + d0, acc);
+}
+
+}  // namespace b200

@@ -1,0 +1,209 @@
+"""Parity of the sm_100a paged attention against the fp32 oracle (GPU).
+
+Cases follow the reference's own unit test (tests/test_paged_split_kv.py:105-114:
+three shape sets x splits 4 and 8, permuted block table) plus the edge cases
+of its semantics: partial last pages, rows whose split holds no key, decode
+rows (q_len = 1), empty requests, seqused_k < q_len, int64 indices, fp16,
+other GQA ratios, page size 32, strided q, and NaN garbage in page tails.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from helpers import ATOL_MAX, ATOL_MEAN, assert_close, errors, oracle, row_subset_batch, run_gpu, small_batch
+from minicpm_b200 import _lib, iluvatar_attention, paged_split_kv_attention, split_kv_combine
+from minicpm_b200.workloads import build_attention_batch, correctness_batch, lengths_chunked_4k, lengths_chunked_16k
+
+pytestmark = pytest.mark.gpu
+
+REFERENCE_CASES = [
+    ([1, 17, 65], [127, 111, 63]),
+    ([31, 1, 13], [0, 255, 1001]),
+    ([64, 1, 1], [2048, 4096, 8192]),
+]
+
+
+def _no_device_error():
+    assert _lib.device_error() == _lib.DEVERR_NONE
+
+
+@pytest.mark.parametrize("case", range(3))
+@pytest.mark.parametrize("splits", [4, 8, 1, 0])
+def test_reference_unit_cases(case, splits):
+    ql, pre = REFERENCE_CASES[case]
+    batch = small_batch(ql, pre, seed=20260928 + case)
+    got = run_gpu(batch, splits)
+    assert_close(got, oracle(batch).to(torch.bfloat16), f"case{case} S={splits}")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("splits", [1, 2, 4, 8, 16, 0])
+def test_correctness_config(splits):
+    batch = correctness_batch()
+    got = run_gpu(batch, splits)
+    assert_close(got, oracle(batch), f"correctness S={splits}")
+    _no_device_error()
+
+
+def test_edge_lengths():
+    # KV lengths around page and tile boundaries, decode rows, a 1-token
+    # sequence, and query chunks that end mid-tile.
+    ql = [1, 1, 2, 15, 16, 17, 127, 128, 129, 1, 300]
+    pre = [0, 15, 14, 1, 0, 111, 1, 128, 127, 4095, 17]
+    batch = small_batch(ql, pre, seed=7, pool_pages=400)
+    want = oracle(batch)
+    for s in (1, 2, 4, 16):
+        assert_close(run_gpu(batch, s), want, f"edges S={s}")
+    _no_device_error()
+
+
+def test_empty_request_and_no_key_rows():
+    # Request 1 has no query rows; request 2 has seqused_k < q_len so its
+    # first rows see no key (they are 0, as the kernel's acc / max(l, 1e-20)).
+    batch = build_attention_batch([5, 0, 20], [40, 10, 12], seed=3)
+    want = oracle(batch)
+    for s in (1, 4):
+        got = run_gpu(batch, s)
+        assert_close(got, want, f"empty/no-key S={s}")
+        assert got[5:13].abs().max().item() == 0.0
+    _no_device_error()
+
+
+def test_nan_in_page_tail_is_ignored():
+    batch = small_batch([9, 30], [20, 3], seed=11, pool_pages=8)
+    want = oracle(batch)
+    cache = batch.kv_cache.clone()
+    for row, L in enumerate(batch.kv_lens):
+        last = int(batch.block_table[row, (L - 1) // 16])
+        cache[last, :, L % 16 :] = float("nan")
+        # Pages that belong to nobody hold NaN too.
+    used = set(batch.block_table.flatten().tolist())
+    for p in range(cache.shape[0]):
+        if p not in used:
+            cache[p] = float("nan")
+    batch.kv_cache = cache
+    for s in (1, 2):
+        assert_close(run_gpu(batch, s), want, f"nan tail S={s}")
+
+
+def test_int64_indices_and_wide_table():
+    batch = small_batch([33, 7], [100, 500], seed=5, extra_table_cols=9)
+    want = oracle(batch)
+    b = batch.to("cuda")
+    out = torch.empty_like(b.q)
+    paged_split_kv_attention(
+        b.q, b.kv_cache[:, 0], b.kv_cache[:, 1], out, b.block_table.long(), b.seqused_k.long(), b.cu_seqlens_q.long(),
+        b.max_seqlen_q, b.max_seqlen_k, b.softmax_scale, num_splits=2,
+    )
+    assert_close(out.cpu(), want, "int64")
+
+
+def test_fp16():
+    batch = small_batch([40, 3], [200, 77], seed=9, dtype=torch.float16)
+    got = run_gpu(batch, 1)
+    assert got.dtype == torch.float16
+    assert_close(got, oracle(batch), "fp16")
+
+
+@pytest.mark.parametrize("hq,hkv", [(8, 1), (16, 16), (32, 2), (4, 2)])
+def test_other_gqa_ratios(hq, hkv):
+    batch = small_batch([19, 70], [45, 300], seed=13, num_q_heads=hq, num_kv_heads=hkv)
+    for s in (1, 4):
+        assert_close(run_gpu(batch, s), oracle(batch), f"gqa {hq}/{hkv} S={s}")
+
+
+def test_page_size_32():
+    batch = small_batch([50, 9], [77, 400], seed=17, block_size=32)
+    assert_close(run_gpu(batch, 2), oracle(batch), "bs32")
+
+
+def test_strided_query_and_5d_cache_through_dispatcher(monkeypatch):
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    monkeypatch.setenv("ILUVATAR_NUM_SPLITS", "4")
+    batch = small_batch([21, 40], [10, 200], seed=19)
+    want = oracle(batch)
+    b = batch.to("cuda")
+    # q as a view into a wider [T, H + 2*KH, D] qkv buffer.
+    qkv = torch.randn(b.q.shape[0], 16 + 4, 128, device="cuda", dtype=torch.bfloat16)
+    qkv[:, :16] = b.q
+    q = qkv[:, :16]
+    out = torch.empty(b.q.shape, device="cuda", dtype=torch.bfloat16)
+    ret = iluvatar_attention(
+        q, b.kv_cache, b.kv_cache, out, b.cu_seqlens_q, b.max_seqlen_q, b.seqused_k, b.max_seqlen_k,
+        b.softmax_scale, causal=True, block_table=b.block_table,
+    )
+    assert ret is out
+    assert_close(out.cpu(), want, "dispatcher 5-D cache")
+
+
+def test_zero_lengths_return_zeros():
+    batch = small_batch([4], [4], seed=1).to("cuda")
+    out = torch.full_like(batch.q, 3.0)
+    ret = paged_split_kv_attention(
+        batch.q, batch.kv_cache[:, 0], batch.kv_cache[:, 1], out, batch.block_table, batch.seqused_k,
+        batch.cu_seqlens_q, 0, batch.max_seqlen_k, batch.softmax_scale,
+    )
+    assert ret is out and out.abs().max().item() == 0.0
+
+
+def test_deterministic_and_page_permutation_invariant():
+    q, kv = lengths_chunked_4k(num_seqs=6)
+    batch = build_attention_batch(q, kv, seed=23)
+    a = run_gpu(batch, 1)
+    b = run_gpu(batch, 1)
+    assert torch.equal(a, b)
+    # Move every page to a new physical slot: the output must not change at all.
+    perm = torch.randperm(batch.kv_cache.shape[0], generator=torch.Generator().manual_seed(5))
+    moved = batch.kv_cache.clone()
+    moved[perm] = batch.kv_cache
+    batch2 = build_attention_batch(q, kv, seed=23)
+    batch2.kv_cache = moved
+    batch2.block_table = perm[batch.block_table.long()].to(torch.int32)
+    assert torch.equal(run_gpu(batch2, 1), a)
+
+
+def test_chunked_prefill_4k_subset_against_oracle():
+    q, kv = lengths_chunked_4k()
+    batch = build_attention_batch(q[:6], kv[:6], seed=29)
+    want = oracle(batch)
+    for s in (1, 4, 8, 0):
+        assert_close(run_gpu(batch, s), want, f"4k subset S={s}")
+    _no_device_error()
+
+
+def test_full_16k_config_sampled_rows_and_split_invariance():
+    """The 16K config at full size: sampled rows against the oracle, and
+    S = 1 / 4 / 8 agree with each other (a size-independent property)."""
+    q, kv = lengths_chunked_16k()
+    batch = build_attention_batch(q, kv)
+    outs = {s: run_gpu(batch, s) for s in (1, 4, 8)}
+    for s in (4, 8):
+        mx, mn = errors(outs[s], outs[1])
+        assert mx <= ATOL_MAX and mn <= 2e-4, (s, mx, mn)
+    for seq in (0, 31, 63):
+        for r0, r1 in ((0, 16), (1000, 1040), (2040, 2048)):
+            sub, rows = row_subset_batch(batch, seq, r0, r1)
+            assert_close(outs[1][rows], oracle(sub), f"16k seq{seq} rows{r0}:{r1}")
+    _no_device_error()
+
+
+def test_split_combine_matches_reference_reduce(golden_dir):
+    import numpy as np
+
+    rec = np.load(golden_dir / "attn_small_b.npz")
+    for s in rec["splits"].tolist():
+        o = torch.from_numpy(rec[f"o_split_s{s}"]).cuda()
+        m = torch.from_numpy(rec[f"m_split_s{s}"]).cuda()
+        l = torch.from_numpy(rec[f"l_split_s{s}"]).cuda()
+        want = torch.from_numpy(rec[f"reduce_s{s}"])
+        out = torch.empty(o.shape[1:], device="cuda", dtype=torch.float32)
+        split_kv_combine(o, m, l, out)
+        assert (out.cpu() - want).abs().max().item() < 2e-6
+        out16 = torch.empty(o.shape[1:], device="cuda", dtype=torch.bfloat16)
+        split_kv_combine(o.to(torch.bfloat16), m, l, out16)
+        assert (out16.cpu().float() - want).abs().max().item() < 2e-2

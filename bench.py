@@ -50,6 +50,8 @@ def parse_args():
     ap.add_argument("--workload", default="chunked_prefill_16k",
                     choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "rope_16384"])
     ap.add_argument("--splits", type=int, default=0, help="0 = automatic")
+    ap.add_argument("--num-seqs", type=int, default=0,
+                    help="keep only the first N sequences of the workload (small cases for profiling)")
     ap.add_argument("--rotary-dim", type=int, default=128)
     ap.add_argument("--interleaved", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -187,11 +189,13 @@ def shard(n: int, world: int, rank: int) -> list[int]:
     return contiguous_shard(n, world, rank)
 
 
-def build_local_batch(workload: str, world: int, rank: int):
+def build_local_batch(workload: str, world: int, rank: int, num_seqs: int = 0):
     from minicpm_b200 import workloads
     from minicpm_b200.sharding import lpt_shard
 
     q, kv = workloads.WORKLOADS[workload]()
+    if num_seqs:
+        q, kv = q[:num_seqs], kv[:num_seqs]
     if workload == "mixed_256":
         ids = lpt_shard(q, kv, world, 16, 128)[rank]
     else:
@@ -312,7 +316,7 @@ def attention_bench(args, world, rank, local):
     from oracle import causal_flops  # FLOP formula of the reference harness (no compute)
 
     dev = torch.device("cuda", local)
-    batch, all_q, all_kv = build_local_batch(args.workload, world, rank)
+    batch, all_q, all_kv = build_local_batch(args.workload, world, rank, args.num_seqs)
     local_flops = causal_flops(batch.query_lens, batch.kv_lens, 16, 128)
     total_flops = sum_over_ranks(float(local_flops), world) if world > 1 else float(local_flops)
     total_tokens = sum(all_q)

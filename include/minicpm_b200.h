@@ -125,6 +125,25 @@ B200_API int32_t b200_choose_num_splits(int32_t total_q, int32_t num_seqs, int32
 B200_API int b200_paged_attn_fwd(const B200AttnParams* params, void* stream);
 
 /*
+ * b200_paged_attn_fwd without a caller-supplied workspace: no counterpart in
+ * the reference.  For callers that cannot allocate device memory at call time
+ * (an engine that reserved HBM for its KV cache up front, a foreign-language
+ * host without a device allocator, a path where cudaMalloc's implicit device
+ * synchronisation is not acceptable).  params->workspace and
+ * params->workspace_bytes are ignored; the scratch is one file-scope device
+ * array of B200_STATIC_SCRATCH_BYTES, held by every GPU that loads this
+ * library until the process exits.  Calls whose scratch need
+ * (b200_attn_workspace_bytes) exceeds it fail with B200_ERR_INVALID.  The
+ * first call on a device looks up the array's device address (make it before
+ * any stream capture).  All calls on a device share the array: calls that
+ * overlap on the GPU (other streams, other threads) race and must not be
+ * issued.  No scratch byte needs to start at zero; every byte a call reads
+ * it wrote first.  Allocates nothing.
+ */
+#define B200_STATIC_SCRATCH_BYTES (32u << 20)
+B200_API int b200_paged_attn_fwd_noalloc(const B200AttnParams* params, void* stream);
+
+/*
  * Cross-split combine: out[t,h,:] = sum_s w_s O_s[t,h,:] / max(sum_s w_s, 1e-20),
  * w_s = exp(m_s - max_s m_s) * l_s for l_s > 0, else 0.
  * o_splits [num_splits, total_q, num_heads, head_dim] (F16 / BF16 / F32), m, l

@@ -420,3 +420,65 @@ int b200_device_error(void* stream, uint32_t* code) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of b200_paged_attn_fwd.
+//
+// Some callers cannot hand this library a workspace: a serving engine that
+// reserved nearly all of HBM for its KV-cache pages at start-up and forbids
+// later allocations, a host runtime in another language that reaches this
+// code through the C ABI and has no device allocator of its own, or a caller
+// on a latency-critical path where cudaMalloc/cudaFree would synchronise the
+// device.  For them the scratch (work list, per-sequence tile offsets and,
+// when the KV axis is split, the partial outputs and their m/l statistics)
+// lives in one file-scope device array of B200_STATIC_SCRATCH_BYTES, which
+// every GPU that loads this library holds until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = B200_STATIC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_ptr[kMaxDevices] = {};
+
+}  // namespace
+
+extern "C" {
+
+int b200_paged_attn_fwd_noalloc(const B200AttnParams* p, void* stream) {
+  if (!p) return fail(B200_ERR_INVALID, "null params");
+  // Size check first: pure host arithmetic, identical to the workspace query.
+  const size_t need = b200_attn_workspace_bytes(p->total_q, p->num_seqs, p->num_q_heads, p->num_kv_heads,
+                                                p->head_dim, p->num_splits, p->max_seqlen_k, p->dtype);
+  if (need > kStaticScratchBytes)
+    return fail(B200_ERR_INVALID,
+                "b200_paged_attn_fwd_noalloc: this call needs %zu bytes of scratch but the static scratch holds "
+                "%zu; use b200_paged_attn_fwd with a caller-owned workspace (or fewer splits)",
+                need, kStaticScratchBytes);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(B200_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    // Set-up, once per device, with that device current: the host-side name
+    // g_static_scratch is only a stand-in, the kernel needs the device address.
+    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+    if (!g_static_scratch_ptr[dev]) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+      if (e != cudaSuccess || !ptr)
+        return fail(B200_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+      g_static_scratch_ptr[dev] = ptr;
+    }
+    scratch = g_static_scratch_ptr[dev];
+  }
+  B200AttnParams q = *p;
+  q.workspace = scratch;
+  q.workspace_bytes = kStaticScratchBytes;
+  return b200_paged_attn_fwd(&q, stream);
+}
+
+}  // extern "C"

@@ -87,8 +87,8 @@ WorkspaceLayout attn_workspace_layout(int64_t total_q, int num_seqs, int hq, int
                                       int elt) {
   WorkspaceLayout w{};
   const int group = hkv > 0 ? hq / hkv : 1;
-  const int ppt = group > 0 ? b200::kAttnTileM / group : 1;
-  const int64_t tiles_ub = (total_q + ppt - 1) / (ppt > 0 ? ppt : 1) + num_seqs;
+  const int ppu = (group > 0 ? b200::kAttnTileM / group : 1) * b200::kAttnTilesPerUnit;
+  const int64_t tiles_ub = (total_q + ppu - 1) / (ppu > 0 ? ppu : 1) + num_seqs;
   const int64_t cap = tiles_ub * hkv * splits;
   w.capacity = static_cast<int>(cap > 0x7fffffff ? 0x7fffffff : cap);
   w.count_off = 0;
@@ -257,7 +257,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   sa.seqused = p->seqused_k;
   sa.len_i64 = p->seqlen_dtype == B200_DTYPE_I64;
   sa.num_seqs = p->num_seqs;
-  sa.pos_per_tile = ppt;
+  sa.pos_per_unit = ppt * b200::kAttnTilesPerUnit;
   sa.num_kv_heads = p->num_kv_heads;
   sa.num_splits = splits;
   sa.capacity = w.capacity;
@@ -293,15 +293,21 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
   const dim3 grid(static_cast<unsigned>(w.capacity));
-  if (p->dtype == B200_DTYPE_BF16) {
-    auto k = b200::paged_attn_fwd_kernel<__nv_bfloat16>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kAttnSmemAlloc);
-    k<<<grid, b200::kAttnThreads, b200::kAttnSmemAlloc, s>>>(tm_q, tm_k, tm_v, a);
-  } else {
-    auto k = b200::paged_attn_fwd_kernel<__half>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kAttnSmemAlloc);
-    k<<<grid, b200::kAttnThreads, b200::kAttnSmemAlloc, s>>>(tm_q, tm_k, tm_v, a);
-  }
+  auto launch = [&](auto kernel) -> int {
+    // The kernel rebalances registers between warpgroups with setmaxnreg; the
+    // split adds up only if every thread was launched with exactly
+    // kAttnLaunchRegs registers, so refuse to launch otherwise.
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess || fa.numRegs != b200::kAttnLaunchRegs)
+      return fail(B200_ERR_CUDA, "paged_attn_fwd_kernel built with %d registers per thread, %d expected", fa.numRegs,
+                  b200::kAttnLaunchRegs);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kAttnSmemAlloc);
+    kernel<<<grid, b200::kAttnThreads, b200::kAttnSmemAlloc, s>>>(tm_q, tm_k, tm_v, a);
+    return B200_OK;
+  };
+  const int lr = (p->dtype == B200_DTYPE_BF16) ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16>)
+                                               : launch(b200::paged_attn_fwd_kernel<__half>);
+  if (lr != B200_OK) return lr;
   if (int r = check_launch("paged_attn_fwd_kernel")) return r;
 
   if (splits > 1) {

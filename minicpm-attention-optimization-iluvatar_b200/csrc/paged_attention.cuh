@@ -5,28 +5,40 @@
 //   * query row i of sequence b sits at absolute position L_b - q_len_b + i;
 //   * split s of S covers keys [s * ceil(L/S), min((s + 1) * ceil(L/S), L));
 //   * a key is valid for a row iff it is inside the split and <= the row's
-//     absolute position; a row with no valid key keeps m = -inf, l = 0, O = 0;
+//     absolute position; a row with no valid key keeps l = 0 and O = 0;
 //   * S == 1 writes the normalised output directly; S > 1 writes the
 //     normalised partial O (in the query dtype) plus m (natural-log units)
 //     and l, which b200_split_combine reduces.
 //
-// Work unit = (sequence, KV head, query tile, split).  A query tile packs
-// the G = Hq / KH query heads that share one KV head with 128 / G query
+// Work unit = (sequence, KV head, query-tile pair, split).  A query tile packs
+// the G = Hq / KH query heads that share one KV head with P = 128 / G query
 // positions into the 128 rows of one UMMA M dimension (row r = position
-// r / G, head r % G), so every K/V tile fetched from HBM feeds all G heads.
+// r / G, head r % G), so every K/V tile fetched feeds all G heads.  A unit
+// holds two such tiles (2P consecutive positions, 256 rows) that share every
+// K/V tile; the second is skipped when the sequence has no rows for it.
 //
-// One CTA per unit, 6 warps:
-//   warp 0      TMA producer: Q once, then K and V tiles of 128 tokens as
-//               8 page slices of 16 tokens x 2 half-rows each, addressed
-//               through the block table (per-page TMA gather).  Slices past
-//               the unit's last key load from an out-of-range page index, so
-//               TMA fills zeros and never touches memory outside the cache.
-//   warp 1      TMEM owner and single-thread UMMA issuer:
-//               S[j%2] = Q K_j^T (M128 N128 K128), O += P_{j-1} V_{j-1}.
-//   warps 2..5  softmax warpgroup, one query row per thread: reads S from
-//               TMEM, masks, online softmax in base 2, rescales O in TMEM,
-//               writes P (bf16/f16) to shared memory, final normalise+store.
-// TMEM: S double buffer at columns [0,128) and [128,256), O at [256,384).
+// One CTA per unit, 12 warps in 3 warpgroups:
+//   warp 0      TMA producer: Q0/Q1 once, then K_j and V_j tiles of 128 tokens
+//               into a 5-slot ring, each tile as 8 page slices of 16 tokens x
+//               2 half-rows (a per-page gather through the block table).
+//               Slices past the unit's last key use an out-of-range page
+//               index, so TMA fills zeros and reads nothing outside the cache.
+//   warp 1      TMEM owner and single-thread UMMA issuer, in the order
+//               S0(j+1) = Q0 K^T after PV0(j), S1(j+1) after PV1(j), so each
+//               softmax warpgroup works while the tensor core runs the other
+//               tile's MMAs.  O_t += P_t V with P read from TMEM (TS form).
+//   warps 2..3  idle (they complete the first warpgroup for setmaxnreg)
+//   warps 4..7  softmax warpgroup of tile 0, warps 8..11 of tile 1; one query
+//               row per thread: S row from TMEM, mask, online softmax in base
+//               2, P (bf16/f16) written back over the S columns in TMEM.  The
+//               running maximum is raised only when a row maximum grows by
+//               more than 2^8; only then is O rescaled (rare after the first
+//               tile).  Final normalise and store.
+// TMEM: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512); P_t in the
+// first 64 columns of S_t.
+// Registers: launched at 168 per thread (the 384-thread limit); the first
+// warpgroup gives back down to 104 and the softmax warpgroups take 200 each
+// (104 + 2 x 200 = 3 x 168, the launch's total).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -42,33 +54,34 @@ constexpr int kAttnTileM = 128;   // rows per query tile
 constexpr int kAttnTileN = 128;   // KV tokens per tile
 constexpr int kAttnHeadDim = 128; // head_dim handled by this kernel
 constexpr int kAttnSlice = 16;    // KV tokens per TMA box (page slice)
-constexpr int kAttnThreads = 192;
+constexpr int kAttnTilesPerUnit = 2;
+constexpr int kAttnThreads = 384;
+constexpr int kAttnLaunchRegs = 168;   // 65536 / 384 rounded down to a multiple of 8
+constexpr int kAttnProducerRegs = 104;
+constexpr int kAttnSoftmaxRegs = 200;
+static_assert(kAttnProducerRegs + 2 * kAttnSoftmaxRegs == 3 * kAttnLaunchRegs, "register split");
 constexpr int kAttnTmemCols = 512;
-constexpr int kColS0 = 0, kColS1 = 128, kColO = 256;
+constexpr int kKvStages = 5;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
 
 // Shared memory map (offsets from a 1024-aligned base).
-constexpr uint32_t kSmQ = 0;                       // 2 x 16 KB (d halves)
-constexpr uint32_t kSmK = 32768;                   // 2 stages x 2 halves x 16 KB
-constexpr uint32_t kSmV = kSmK + 65536;            // 2 stages x 2 halves x 16 KB
-constexpr uint32_t kSmP = kSmV + 65536;            // 2 x 16 KB (kv halves)
-constexpr uint32_t kSmBar = kSmP + 32768;          // mbarriers
+constexpr uint32_t kSmQ = 0;                            // Q0, Q1: 2 x (2 x 16 KB)
+constexpr uint32_t kSmKV = 65536;                       // ring: kKvStages x 32 KB
+constexpr uint32_t kSmBar = kSmKV + kKvStages * 32768;  // mbarriers
 constexpr uint32_t kSmBytes = kSmBar + 256;
-constexpr uint32_t kAttnSmemAlloc = kSmBytes + 1024;  // + alignment slack
+constexpr uint32_t kAttnSmemAlloc = kSmBytes + 1024;    // + alignment slack
 
-// mbarrier slots
 enum : int {
   BAR_Q = 0,
-  BAR_K_FULL = 1,   // +stage
-  BAR_K_EMPTY = 3,  // +stage
-  BAR_V_FULL = 5,   // +stage
-  BAR_V_EMPTY = 7,  // +stage
-  BAR_S_FULL = 9,   // +stage
-  BAR_S_FREE = 11,  // +stage
-  BAR_P_FULL = 13,
-  BAR_O_DONE = 14,
-  BAR_DRAIN = 15,
-  BAR_COUNT = 16
+  BAR_KV_FULL = 1,                           // + slot
+  BAR_KV_EMPTY = BAR_KV_FULL + kKvStages,    // + slot
+  BAR_S_FULL = BAR_KV_EMPTY + kKvStages,     // + tile
+  BAR_P_FULL = BAR_S_FULL + 2,               // + tile
+  BAR_O_DONE = BAR_P_FULL + 2,               // + tile
+  BAR_DRAIN = BAR_O_DONE + 2,
+  BAR_COUNT = BAR_DRAIN + 1
 };
+static_assert(BAR_COUNT * 8 + 8 <= 256, "barrier area");
 
 struct AttnKernelArgs {
   const void* block_table;
@@ -88,7 +101,7 @@ struct AttnKernelArgs {
   int total_q;
   int num_q_heads;
   int group;          // G = Hq / KH
-  int pos_per_tile;   // 128 / G
+  int pos_per_tile;   // P = 128 / G
   int block_size;
   int num_blocks;
   int num_splits;
@@ -99,7 +112,8 @@ __device__ __forceinline__ int load_index(const void* p, int64_t i, int is_i64) 
   return is_i64 ? static_cast<int>(static_cast<const int64_t*>(p)[i]) : static_cast<const int*>(p)[i];
 }
 
-// Geometry of one work unit; shared by the scheduler (cost) and the kernel.
+// Geometry of one work unit (pos_per_unit consecutive query positions);
+// shared by the scheduler (cost) and the kernel.
 struct UnitGeom {
   int q_begin, q_len, seq_len;
   int pos0, split_begin, split_end;
@@ -107,14 +121,14 @@ struct UnitGeom {
   int q_abs_min;
 };
 
-__device__ __forceinline__ UnitGeom unit_geometry(int q_begin, int q_end, int seq_len, int qtile, int split,
-                                                  int pos_per_tile, int num_splits) {
+__device__ __forceinline__ UnitGeom unit_geometry(int q_begin, int q_end, int seq_len, int qunit, int split,
+                                                  int pos_per_unit, int num_splits) {
   UnitGeom u;
   u.q_begin = q_begin;
   u.q_len = q_end - q_begin;
   u.seq_len = seq_len;
-  u.pos0 = qtile * pos_per_tile;
-  const int rows = min(pos_per_tile, u.q_len - u.pos0);
+  u.pos0 = qunit * pos_per_unit;
+  const int rows = min(pos_per_unit, u.q_len - u.pos0);
   u.q_abs_min = seq_len - u.q_len + u.pos0;
   const int q_abs_max = u.q_abs_min + rows - 1;
   const int L = max(seq_len, 0);
@@ -144,8 +158,8 @@ struct Pack2<__half> {
   }
 };
 
-// Wait without the abort short-cut: used on the abort path to let copies
-// and MMAs already in flight land before the CTA exits.
+// Wait without the abort short-cut: used to let copies and MMAs already in
+// flight land before the CTA exits.
 __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
@@ -173,26 +187,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const int P = a.pos_per_tile;
 
   const int4 unit = a.units[blockIdx.x];
-  const int seq = unit.x, qtile = unit.y, kvh = unit.z, split = unit.w;
+  const int seq = unit.x, qunit = unit.y, kvh = unit.z, split = unit.w;
   const UnitGeom ug = unit_geometry(load_index(a.cu_q, seq, a.len_i64), load_index(a.cu_q, seq + 1, a.len_i64),
-                                    load_index(a.seqused, seq, a.len_i64), qtile, split, a.pos_per_tile,
+                                    load_index(a.seqused, seq, a.len_i64), qunit, split, kAttnTilesPerUnit * P,
                                     a.num_splits);
   const int n_tiles = ug.n_tiles;
+  const bool two = ug.pos0 + P < ug.q_len;  // the second query tile has rows
 
   if (threadIdx.x == 0) {
     mbar_init(bar(BAR_Q), 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(BAR_K_FULL + s), 1);
-      mbar_init(bar(BAR_K_EMPTY + s), 1);
-      mbar_init(bar(BAR_V_FULL + s), 1);
-      mbar_init(bar(BAR_V_EMPTY + s), 1);
-      mbar_init(bar(BAR_S_FULL + s), 1);
-      mbar_init(bar(BAR_S_FREE + s), 4);
+    for (int s = 0; s < kKvStages; ++s) {
+      mbar_init(bar(BAR_KV_FULL + s), 1);
+      mbar_init(bar(BAR_KV_EMPTY + s), 1);
     }
-    mbar_init(bar(BAR_P_FULL), 4);
-    mbar_init(bar(BAR_O_DONE), 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(BAR_S_FULL + t), 1);
+      mbar_init(bar(BAR_P_FULL + t), 4);
+      mbar_init(bar(BAR_O_DONE + t), 1);
+    }
     mbar_init(bar(BAR_DRAIN), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -206,295 +221,295 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && n_tiles > 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttnProducerRegs));
+    if (warp == 0 && lane == 0 && n_tiles > 0) {
+      // ---------------------------------------------------------- producer
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       const int head0 = kvh * a.group;
       const int t0 = ug.q_begin + ug.pos0;
-      mbar_arrive_expect_tx(bar(BAR_Q), 2 * 16384);
+      mbar_arrive_expect_tx(bar(BAR_Q), (two ? 2 : 1) * 32768);
       tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q), 0, head0, t0);
       tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q), 64, head0, t0);
-      int kfills[2] = {0, 0}, vfills[2] = {0, 0};
+      if (two) {
+        tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q), 0, head0, t0 + P);
+        tma_load_3d(sbase + kSmQ + 49152, &tm_q, bar(BAR_Q), 64, head0, t0 + P);
+      }
+      int issued = 0;  // ring fills issued so far (fill idx uses slot idx % kKvStages)
       const int64_t bt_row = static_cast<int64_t>(seq) * a.bt_stride;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int tile_start = ug.kv_lo + j * kAttnTileN;
-        int page[8], off[8];
+      int page[8], off[8];
+      for (int idx = 0; idx < 2 * n_tiles; ++idx) {
+        const int j = idx >> 1;
+        const bool is_v = idx & 1;
+        const int slot = idx % kKvStages;
+        const uint32_t ph = (idx / kKvStages) & 1;
+        if (!is_v) {
+          const int tile_start = ug.kv_lo + j * kAttnTileN;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const int pos = tile_start + c * kAttnSlice;
-          page[c] = a.num_blocks;  // out of range: TMA fills zeros
-          off[c] = 0;
-          if (pos < ug.kv_hi) {
-            const int lp = pos / a.block_size;
-            off[c] = pos - lp * a.block_size;
-            if (lp < a.bt_cols) page[c] = load_index(a.block_table, bt_row + lp, a.bt_i64);
+          for (int c = 0; c < 8; ++c) {
+            const int pos = tile_start + c * kAttnSlice;
+            page[c] = a.num_blocks;  // out of range: TMA fills zeros
+            off[c] = 0;
+            if (pos < ug.kv_hi) {
+              const int lp = pos / a.block_size;
+              off[c] = pos - lp * a.block_size;
+              if (lp < a.bt_cols) page[c] = load_index(a.block_table, bt_row + lp, a.bt_i64);
+            }
           }
         }
-        if (!mbar_wait(bar(BAR_K_EMPTY + st), ph ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(bar(BAR_K_FULL + st), 2 * 16384);
-        const uint32_t kdst = sbase + kSmK + st * 32768;
+        if (!mbar_wait(bar(BAR_KV_EMPTY + slot), ph ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), 32768);
+        const uint32_t dst = sbase + kSmKV + slot * 32768;
+        const void* map = is_v ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          tma_load_4d(kdst + c * 2048, &tm_k, bar(BAR_K_FULL + st), 0, off[c], kvh, page[c]);
-          tma_load_4d(kdst + 16384 + c * 2048, &tm_k, bar(BAR_K_FULL + st), 64, off[c], kvh, page[c]);
+          tma_load_4d(dst + c * 2048, map, bar(BAR_KV_FULL + slot), 0, off[c], kvh, page[c]);
+          tma_load_4d(dst + 16384 + c * 2048, map, bar(BAR_KV_FULL + slot), 64, off[c], kvh, page[c]);
         }
-        ++kfills[st];
-        if (!mbar_wait(bar(BAR_V_EMPTY + st), ph ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(bar(BAR_V_FULL + st), 2 * 16384);
-        const uint32_t vdst = sbase + kSmV + st * 32768;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          tma_load_4d(vdst + c * 2048, &tm_v, bar(BAR_V_FULL + st), 0, off[c], kvh, page[c]);
-          tma_load_4d(vdst + 16384 + c * 2048, &tm_v, bar(BAR_V_FULL + st), 64, off[c], kvh, page[c]);
-        }
-        ++vfills[st];
+        ++issued;
       }
-      if (*abort_flag) {
-        // Let every issued copy land before the CTA can exit.
-        mbar_wait_drain(bar(BAR_Q), 0);
-        for (int st = 0; st < 2; ++st) {
-          if (kfills[st] > 0) mbar_wait_drain(bar(BAR_K_FULL + st), (kfills[st] - 1) & 1);
-          if (vfills[st] > 0) mbar_wait_drain(bar(BAR_V_FULL + st), (vfills[st] - 1) & 1);
-        }
-      } else {
-        // Producer tail: the UMMA commits that release the last K and V stages
-        // must have arrived before this CTA's shared memory can be reused.
-        for (int st = 0; st < 2; ++st) {
-          if (kfills[st] > 0) mbar_wait_drain(bar(BAR_K_EMPTY + st), (kfills[st] - 1) & 1);
-          if (vfills[st] > 0) mbar_wait_drain(bar(BAR_V_EMPTY + st), (vfills[st] - 1) & 1);
-        }
+      // Tail: every issued copy must land, and the UMMA commits that release
+      // the slots must arrive, before this CTA's shared memory is reused.
+      mbar_wait_drain(bar(BAR_Q), 0);
+      for (int s = 0; s < kKvStages && s < issued; ++s) {
+        const int last_idx = s + kKvStages * ((issued - 1 - s) / kKvStages);
+        const uint32_t last = (last_idx / kKvStages) & 1;
+        mbar_wait_drain(bar(BAR_KV_FULL + s), last);
+        if (!*abort_flag) mbar_wait_drain(bar(BAR_KV_EMPTY + s), last);
       }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_tiles > 0) {
+    } else if (warp == 1 && lane == 0 && n_tiles > 0) {
+      // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_qk = umma_idesc_f16(kBF16, 128, 128, false, false);
       constexpr uint32_t idesc_pv = umma_idesc_f16(kBF16, 128, 128, false, true);
-      bool ok = mbar_wait(bar(BAR_Q), 0, abort_flag);
-      for (int j = 0; ok && j <= n_tiles; ++j) {
-        if (j < n_tiles) {
-          const int st = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(bar(BAR_K_FULL + st), ph, abort_flag)) break;
-          if (!mbar_wait(bar(BAR_S_FREE + st), ph ^ 1, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t d_s = tmem + (st ? kColS1 : kColS0);
-          const uint32_t kbase = sbase + kSmK + st * 32768;
+      auto issue_s = [&](int t, uint32_t kslot_addr) {
+        const uint32_t q = sbase + kSmQ + t * 32768;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_ss(d_s, umma_desc_sw128(sbase + kSmQ + koff, 16, 1024), umma_desc_sw128(kbase + koff, 16, 1024),
-                    idesc_qk, kk > 0);
-          }
-          tc_commit(bar(BAR_S_FULL + st));
-          tc_commit(bar(BAR_K_EMPTY + st));
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_ss(tmem + t * 128, umma_desc_sw128(q + koff, 16, 1024), umma_desc_sw128(kslot_addr + koff, 16, 1024),
+                  idesc_qk, kk > 0);
         }
-        if (j > 0) {
-          const int i = j - 1;
-          const int st = i & 1;
-          const uint32_t ph = (i >> 1) & 1;
-          if (!mbar_wait(bar(BAR_V_FULL + st), ph, abort_flag)) break;
-          if (!mbar_wait(bar(BAR_P_FULL), i & 1, abort_flag)) break;
-          tc_fence_after();
-          const uint32_t vbase = sbase + kSmV + st * 32768;
+        tc_commit(bar(BAR_S_FULL + t));
+      };
+      auto issue_pv = [&](int t, uint32_t vslot_addr, bool acc) {
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t poff = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_ss(tmem + kColO, umma_desc_sw128(sbase + kSmP + poff, 16, 1024),
-                    umma_desc_sw128(vbase + kk * 2048, 16384, 1024), idesc_pv, (i > 0 || kk > 0));
-          }
-          tc_commit(bar(BAR_O_DONE));
-          tc_commit(bar(BAR_V_EMPTY + st));
+        for (int kk = 0; kk < 8; ++kk) {
+          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, umma_desc_sw128(vslot_addr + kk * 2048, 16384, 1024),
+                  idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
+        tc_commit(bar(BAR_O_DONE + t));
+      };
+      auto slot_addr = [&](int idx) { return sbase + kSmKV + (idx % kKvStages) * 32768; };
+      auto wait_full = [&](int idx) {
+        return mbar_wait(bar(BAR_KV_FULL + idx % kKvStages), (idx / kKvStages) & 1, abort_flag);
+      };
+
+      bool ok = mbar_wait(bar(BAR_Q), 0, abort_flag) && wait_full(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, slot_addr(0));
+        if (two) issue_s(1, slot_addr(0));
+        tc_commit(bar(BAR_KV_EMPTY + 0));
       }
-      if (*abort_flag) {
-        tc_commit(bar(BAR_DRAIN));
-        mbar_wait_drain(bar(BAR_DRAIN), 0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int vidx = 2 * j + 1, kidx = 2 * j + 2;
+        const bool more = j + 1 < n_tiles;
+        if (!wait_full(vidx) || !mbar_wait(bar(BAR_P_FULL + 0), j & 1, abort_flag)) break;
+        tc_fence_after();
+        issue_pv(0, slot_addr(vidx), j > 0);
+        if (more) {
+          if (!wait_full(kidx)) break;
+          tc_fence_after();
+          issue_s(0, slot_addr(kidx));
+        }
+        if (two) {
+          if (!mbar_wait(bar(BAR_P_FULL + 1), j & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_pv(1, slot_addr(vidx), j > 0);
+          if (more) issue_s(1, slot_addr(kidx));
+        }
+        tc_commit(bar(BAR_KV_EMPTY + vidx % kKvStages));
+        if (more) tc_commit(bar(BAR_KV_EMPTY + kidx % kKvStages));
       }
+      // All MMAs issued so far complete before the CTA may free TMEM.
+      tc_commit(bar(BAR_DRAIN));
+      mbar_wait_drain(bar(BAR_DRAIN), 0);
     }
   } else {
-    // ------------------------------------------------------------ softmax
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
-    const int row = quarter * 32 + lane;
-    const int row_pos = ug.pos0 + row / a.group;
-    const int row_head = kvh * a.group + row % a.group;
-    const bool row_valid = row_pos < ug.q_len;
-    const int q_abs = ug.q_abs_min + row / a.group;
-    const int row_hi = min(ug.split_end, q_abs + 1);
-    const int tiles_unmasked_hi = min(ug.split_end, ug.q_abs_min + 1);
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const float sl2 = a.scale_log2;
-    // V rows [v_tail_from, v_tail_to) of the last tile: loaded page rows at or past L.
-    const int last_start = ug.kv_lo + (n_tiles - 1) * kAttnTileN;
-    const int v_tail_from = max(ug.seq_len - last_start, 0);
-    const int v_tail_to = min(((ug.kv_hi + kAttnSlice - 1) / kAttnSlice) * kAttnSlice - last_start, kAttnTileN);
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttnSoftmaxRegs));
+    // ------------------------------------------------------------ softmax (tile t)
+    const int t = (warp - 4) >> 2;
+    if (t == 0 || two) {
+      const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+      const int row = quarter * 32 + lane;
+      const int tile_pos0 = ug.pos0 + t * P;
+      const int row_pos = tile_pos0 + row / a.group;
+      const int row_head = kvh * a.group + row % a.group;
+      const bool row_valid = row_pos < ug.q_len;
+      const int q_abs = ug.q_abs_min + t * P + row / a.group;
+      const int row_hi = min(ug.split_end, q_abs + 1);
+      const int unmasked_hi = min(ug.split_end, ug.q_abs_min + t * P + 1);
+      const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+      const uint32_t s_addr = tmem + lane_base + t * 128;
+      const uint32_t o_addr = tmem + lane_base + 256 + t * 128;
+      const float sl2 = a.scale_log2;
+      // V rows [v_tail_from, v_tail_to) of the last tile: loaded page rows at or past L.
+      const int last_start = ug.kv_lo + (n_tiles - 1) * kAttnTileN;
+      const int v_tail_from = max(ug.seq_len - last_start, 0);
+      const int v_tail_to = min(((ug.kv_hi + kAttnSlice - 1) / kAttnSlice) * kAttnSlice - last_start, kAttnTileN);
 
-    float m2 = -INFINITY;
-    float l = 0.f;
-    bool aborted = false;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait(bar(BAR_S_FULL + st), ph, abort_flag)) {
-        aborted = true;
-        break;
-      }
-      __syncwarp();
-      tc_fence_after();
-      uint32_t sr[4][32];
-      const uint32_t s_addr = tmem + lane_base + (st ? kColS1 : kColS0);
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(s_addr + 32 * c4, sr[c4]);
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_wait_ld(sr[c4]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(BAR_S_FREE + st));
-
-      const int tile_start = ug.kv_lo + j * kAttnTileN;
-      const bool need_mask = (tile_start < ug.split_begin) || (tile_start + kAttnTileN > tiles_unmasked_hi);
-      if (need_mask) {
-        const int lo = ug.split_begin - tile_start;
-        const int hi = row_hi - tile_start;
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int col = c4 * 32 + c;
-            if (col < lo || col >= hi) sr[c4][c] = __float_as_uint(-INFINITY);
-          }
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        mx0 = fmaxf(mx0, __uint_as_float(sr[0][c]));
-        mx1 = fmaxf(mx1, __uint_as_float(sr[1][c]));
-        mx2 = fmaxf(mx2, __uint_as_float(sr[2][c]));
-        mx3 = fmaxf(mx3, __uint_as_float(sr[3][c]));
-      }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-      const float m_new = fmaxf(m2, mx * sl2);
-      const float safe = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2_approx(m2 - safe);
-      const float neg_safe = -safe;
-
-      uint32_t pk[64];
-      float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c4][c]), sl2, neg_safe));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c4][c + 1]), sl2, neg_safe));
-          if (c & 2) {
-            sum2 += p0;
-            sum3 += p1;
-          } else {
-            sum0 += p0;
-            sum1 += p1;
-          }
-          pk[c4 * 16 + c / 2] = Pack2<T>::pack(p0, p1);
-        }
-      }
-      l = l * alpha + ((sum0 + sum1) + (sum2 + sum3));
-      m2 = m_new;
-
-      if (j > 0) {
-        // PV of the previous tile must be done before O is rescaled and P is overwritten.
-        if (!mbar_wait(bar(BAR_O_DONE), (j - 1) & 1, abort_flag)) {
+      float m_used = -INFINITY;  // running maximum in scaled base-2 units
+      float l = 0.f;
+      bool aborted = false;
+      for (int j = 0; j < n_tiles; ++j) {
+        if (!mbar_wait(bar(BAR_S_FULL + t), j & 1, abort_flag)) {
           aborted = true;
           break;
         }
+        __syncwarp();
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          const uint32_t o_addr = tmem + lane_base + kColO;
+        uint32_t sr[4][32];
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            uint32_t o[32];
+        for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(s_addr + 32 * c4, sr[c4]);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) tmem_wait_ld(sr[c4]);
+
+        const int tile_start = ug.kv_lo + j * kAttnTileN;
+        if (tile_start < ug.split_begin || tile_start + kAttnTileN > unmasked_hi) {
+          const int lo = ug.split_begin - tile_start;
+          const int hi = row_hi - tile_start;
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int col = c4 * 32 + c;
+              if (col < lo || col >= hi) sr[c4][c] = __float_as_uint(-INFINITY);
+            }
+        }
+        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          mx0 = fmaxf(mx0, __uint_as_float(sr[0][c]));
+          mx1 = fmaxf(mx1, __uint_as_float(sr[1][c]));
+          mx2 = fmaxf(mx2, __uint_as_float(sr[2][c]));
+          mx3 = fmaxf(mx3, __uint_as_float(sr[3][c]));
+        }
+        const float m_cand = fmaxf(m_used, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
+        const bool raise = m_cand > m_used + kRescaleThreshold;  // false while both are -inf
+        if (__any_sync(0xffffffffu, raise)) {
+          const float alpha = raise ? ex2_approx(m_used - m_cand) : 1.f;  // 0 when m_used = -inf
+          if (j > 0) {
+            // O holds PV of tiles < j: scale it before PV_j accumulates.
+            if (!mbar_wait(bar(BAR_O_DONE + t), (j - 1) & 1, abort_flag)) {
+              aborted = true;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (int c8 = 0; c8 < 8; ++c8) {
+              uint32_t o[16];
+              tmem_ld16(o_addr + 16 * c8, o);
+              tmem_wait_ld16(o);
+#pragma unroll
+              for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+              tmem_st16(o_addr + 16 * c8, o);
+            }
+          }
+          if (raise) {
+            l *= alpha;
+            m_used = m_cand;
+          }
+        }
+        const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+
+        // P over the first 64 columns of S_t (column c = keys 2c, 2c+1), stored
+        // 16 columns at a time as it is produced; S is already in registers.
+        float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c4][c]), sl2, neg_m));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c4][c + 1]), sl2, neg_m));
+            if (c & 2) {
+              sum2 += p0;
+              sum3 += p1;
+            } else {
+              sum0 += p0;
+              sum1 += p1;
+            }
+            pk[c / 2] = Pack2<T>::pack(p0, p1);
+          }
+          tmem_st16(s_addr + 16 * c4, pk);
+        }
+        l += (sum0 + sum1) + (sum2 + sum3);
+        if (t == 0 && j == n_tiles - 1 && v_tail_from < v_tail_to) {
+          // Rows of the last page past the sequence end may hold anything (NaN
+          // included); P is 0 there but 0 * NaN is NaN, so zero those V rows,
+          // as the reference's masked V load does (triton_split_kv_paged.py:122).
+          const int vidx = 2 * j + 1;
+          if (!mbar_wait(bar(BAR_KV_FULL + vidx % kKvStages), (vidx / kKvStages) & 1, abort_flag)) {
+            aborted = true;
+            break;
+          }
+          const uint32_t vbase = sbase + kSmKV + (vidx % kKvStages) * 32768;
+          const int n16 = (v_tail_to - v_tail_from) * 16;  // 16-byte pieces over both halves
+          for (int i = threadIdx.x - 128; i < n16; i += 128) {
+            const int r = v_tail_from + (i >> 4);
+            const int half = (i >> 3) & 1;
+            st_shared_v4(vbase + half * 16384 + r * 128 + (i & 7) * 16, 0u, 0u, 0u, 0u);
+          }
+          fence_proxy_async_smem();
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(BAR_P_FULL + t));  // one arrival per softmax warp
+      }
+
+      // ---------------------------------------------------------- epilogue
+      if (!aborted && n_tiles > 0) {
+        if (!mbar_wait(bar(BAR_O_DONE + t), (n_tiles - 1) & 1, abort_flag)) aborted = true;
+        tc_fence_after();
+      }
+      if (!aborted) {
+        const float inv = 1.f / fmaxf(l, 1e-20f);
+        const int tok = ug.q_begin + row_pos;
+        T* dst;
+        if (a.num_splits == 1) {
+          dst = static_cast<T*>(a.out) + static_cast<int64_t>(tok) * a.out_st + static_cast<int64_t>(row_head) * a.out_sh;
+        } else {
+          const int64_t rowi = (static_cast<int64_t>(split) * a.total_q + tok) * a.num_q_heads + row_head;
+          dst = static_cast<T*>(a.o_split) + rowi * kAttnHeadDim;
+          if (row_valid) {
+            a.m_split[rowi] = (l > 0.f) ? m_used * 0.69314718055994530942f : -INFINITY;
+            a.l_split[rowi] = l;
+          }
+        }
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t o[32];
+          if (n_tiles > 0) {
             tmem_ld32(o_addr + 32 * c4, o);
             tmem_wait_ld(o);
+          } else {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(o_addr + 32 * c4, o);
+            for (int c = 0; c < 32; ++c) o[c] = 0u;
           }
-          tmem_wait_st();
-        }
-      }
-      // P row -> shared memory, K-major with the 128-byte swizzle (16-byte chunk c of
-      // row r lands at chunk c ^ (r % 8)).
-      const uint32_t p_row = sbase + kSmP + row * 128;
+          if (row_valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const uint32_t addr = p_row + (ch >> 3) * 16384 + (((ch & 7) ^ (row & 7)) << 4);
-        st_shared_v4(addr, pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-      }
-      if (j == n_tiles - 1 && v_tail_from < v_tail_to) {
-        // Rows of the last page past the sequence end may hold anything (NaN
-        // included); P is 0 there but 0 * NaN is NaN, so zero those V rows,
-        // as the reference's masked V load does (triton_split_kv_paged.py:122).
-        if (!mbar_wait(bar(BAR_V_FULL + st), ph, abort_flag)) {
-          aborted = true;
-          break;
-        }
-        const uint32_t vbase = sbase + kSmV + st * 32768;
-        const int n16 = (v_tail_to - v_tail_from) * 16;  // 16-byte pieces over both halves
-        for (int i = threadIdx.x - 64; i < n16; i += 128) {
-          const int r = v_tail_from + (i >> 4);
-          const int half = (i >> 3) & 1;
-          st_shared_v4(vbase + half * 16384 + r * 128 + (i & 7) * 16, 0u, 0u, 0u, 0u);
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(BAR_P_FULL));  // one arrival per softmax warp
-    }
-
-    // ------------------------------------------------------------ epilogue
-    if (!aborted && n_tiles > 0) {
-      if (!mbar_wait(bar(BAR_O_DONE), (n_tiles - 1) & 1, abort_flag)) aborted = true;
-      tc_fence_after();
-    }
-    if (!aborted) {
-      const float inv = 1.f / fmaxf(l, 1e-20f);
-      const int t = ug.q_begin + row_pos;
-      T* dst;
-      if (a.num_splits == 1) {
-        dst = static_cast<T*>(a.out) + static_cast<int64_t>(t) * a.out_st + static_cast<int64_t>(row_head) * a.out_sh;
-      } else {
-        const int64_t rowi = (static_cast<int64_t>(split) * a.total_q + t) * a.num_q_heads + row_head;
-        dst = static_cast<T*>(a.o_split) + rowi * kAttnHeadDim;
-        if (row_valid) {
-          a.m_split[rowi] = (m2 == -INFINITY) ? -INFINITY : m2 * 0.69314718055994530942f;
-          a.l_split[rowi] = l;
-        }
-      }
-      const uint32_t o_addr = tmem + lane_base + kColO;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o[32];
-        if (n_tiles > 0) {
-          tmem_ld32(o_addr + 32 * c4, o);
-          tmem_wait_ld(o);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = 0u;
-        }
-        if (row_valid) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = Pack2<T>::pack(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-            w.y = Pack2<T>::pack(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-            w.z = Pack2<T>::pack(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-            w.w = Pack2<T>::pack(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-            d4[v] = w;
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = Pack2<T>::pack(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+              w.y = Pack2<T>::pack(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+              w.z = Pack2<T>::pack(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+              w.w = Pack2<T>::pack(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+              d4[v] = w;
+            }
           }
         }
       }
@@ -510,6 +525,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
+
 // ---------------------------------------------------------------------------
 // Device-side work list: one block, bucket sort of units by KV-tile count,
 // heaviest first, so the hardware's in-order CTA dispatch approximates a
@@ -524,7 +540,7 @@ struct SchedArgs {
   const void* seqused;
   int len_i64;
   int num_seqs;
-  int pos_per_tile;
+  int pos_per_unit;  // query positions per work unit
   int num_kv_heads;
   int num_splits;
   int capacity;
@@ -571,7 +587,7 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
     int n = 0;
     if (b < a.num_seqs) {
       const int ql = load_index(a.cu_q, b + 1, a.len_i64) - load_index(a.cu_q, b, a.len_i64);
-      n = ql > 0 ? (ql + a.pos_per_tile - 1) / a.pos_per_tile : 0;
+      n = ql > 0 ? (ql + a.pos_per_unit - 1) / a.pos_per_unit : 0;
     }
     int total;
     const int before = block_exclusive_scan(n, warp_sums, total);
@@ -601,7 +617,7 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
     seq = lo;
     qtile = tile - a.tile_base[seq];
     const UnitGeom g = unit_geometry(load_index(a.cu_q, seq, a.len_i64), load_index(a.cu_q, seq + 1, a.len_i64),
-                                     load_index(a.seqused, seq, a.len_i64), qtile, split, a.pos_per_tile,
+                                     load_index(a.seqused, seq, a.len_i64), qtile, split, a.pos_per_unit,
                                      a.num_splits);
     bucket = min(g.n_tiles, kSchedBuckets - 1);
   };

@@ -223,61 +223,78 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttnProducerRegs));
-    if (warp == 0 && lane == 0 && n_tiles > 0) {
-      // ---------------------------------------------------------- producer
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      const int head0 = kvh * a.group;
-      const int t0 = ug.q_begin + ug.pos0;
-      mbar_arrive_expect_tx(bar(BAR_Q), (two ? 2 : 1) * 32768);
-      tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q), 0, head0, t0);
-      tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q), 64, head0, t0);
-      if (two) {
-        tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q), 0, head0, t0 + P);
-        tma_load_3d(sbase + kSmQ + 49152, &tm_q, bar(BAR_Q), 64, head0, t0 + P);
+    if (warp == 0 && n_tiles > 0) {
+      // ---------------------------------------------------------- producer (whole warp)
+      // Lane c < 8 owns page slice c of a tile: it looks up the slice's physical
+      // page one tile ahead (the block-table reads overlap the previous tile's
+      // copies), and lanes 0..15 each issue one of the tile's 16 TMA boxes.
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        const int head0 = kvh * a.group;
+        const int t0 = ug.q_begin + ug.pos0;
+        mbar_arrive_expect_tx(bar(BAR_Q), (two ? 2 : 1) * 32768);
+        tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q), 0, head0, t0);
+        tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q), 64, head0, t0);
+        if (two) {
+          tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q), 0, head0, t0 + P);
+          tma_load_3d(sbase + kSmQ + 49152, &tm_q, bar(BAR_Q), 64, head0, t0 + P);
+        }
       }
-      int issued = 0;  // ring fills issued so far (fill idx uses slot idx % kKvStages)
       const int64_t bt_row = static_cast<int64_t>(seq) * a.bt_stride;
-      int page[8], off[8];
+      const int my_slice = lane & 7;
+      // Page id and in-page offset of slice my_slice of tile j; out-of-range
+      // slices get page num_blocks, which TMA turns into zero fill.
+      auto lookup = [&](int j, int& pg, int& of) {
+        const int pos = ug.kv_lo + j * kAttnTileN + my_slice * kAttnSlice;
+        const int lp = pos / a.block_size;
+        of = pos - lp * a.block_size;
+        const int lpc = min(lp, a.bt_cols - 1);
+        const int v = load_index(a.block_table, bt_row + lpc, a.bt_i64);
+        pg = (pos < ug.kv_hi && lp < a.bt_cols) ? v : a.num_blocks;
+      };
+      int pg_cur, of_cur, pg_nxt = a.num_blocks, of_nxt = 0;
+      lookup(0, pg_cur, of_cur);
+      if (n_tiles > 1) lookup(1, pg_nxt, of_nxt);
+      int issued = 0;  // ring fills issued so far (fill idx uses slot idx % kKvStages)
       for (int idx = 0; idx < 2 * n_tiles; ++idx) {
         const int j = idx >> 1;
         const bool is_v = idx & 1;
         const int slot = idx % kKvStages;
         const uint32_t ph = (idx / kKvStages) & 1;
-        if (!is_v) {
-          const int tile_start = ug.kv_lo + j * kAttnTileN;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int pos = tile_start + c * kAttnSlice;
-            page[c] = a.num_blocks;  // out of range: TMA fills zeros
-            off[c] = 0;
-            if (pos < ug.kv_hi) {
-              const int lp = pos / a.block_size;
-              off[c] = pos - lp * a.block_size;
-              if (lp < a.bt_cols) page[c] = load_index(a.block_table, bt_row + lp, a.bt_i64);
-            }
-          }
+        if (!is_v && j > 0) {
+          pg_cur = pg_nxt;
+          of_cur = of_nxt;
+          if (j + 1 < n_tiles) lookup(j + 1, pg_nxt, of_nxt);
         }
-        if (!mbar_wait(bar(BAR_KV_EMPTY + slot), ph ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), 32768);
-        const uint32_t dst = sbase + kSmKV + slot * 32768;
-        const void* map = is_v ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          tma_load_4d(dst + c * 2048, map, bar(BAR_KV_FULL + slot), 0, off[c], kvh, page[c]);
-          tma_load_4d(dst + 16384 + c * 2048, map, bar(BAR_KV_FULL + slot), 64, off[c], kvh, page[c]);
+        const int c = (lane >> 1) & 7;
+        const int page = __shfl_sync(0xffffffffu, pg_cur, c);
+        const int off = __shfl_sync(0xffffffffu, of_cur, c);
+        int ok = 1;
+        if (lane == 0) {
+          ok = mbar_wait(bar(BAR_KV_EMPTY + slot), ph ^ 1, abort_flag);
+          if (ok) mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), 32768);
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;  // also orders the expect_tx before the copies
+        if (lane < 16) {
+          const int half = lane & 1;
+          const void* map = is_v ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
+          tma_load_4d(sbase + kSmKV + slot * 32768 + half * 16384 + c * 2048, map, bar(BAR_KV_FULL + slot), half * 64,
+                      off, kvh, page);
         }
         ++issued;
       }
       // Tail: every issued copy must land, and the UMMA commits that release
       // the slots must arrive, before this CTA's shared memory is reused.
-      mbar_wait_drain(bar(BAR_Q), 0);
-      for (int s = 0; s < kKvStages && s < issued; ++s) {
-        const int last_idx = s + kKvStages * ((issued - 1 - s) / kKvStages);
-        const uint32_t last = (last_idx / kKvStages) & 1;
-        mbar_wait_drain(bar(BAR_KV_FULL + s), last);
-        if (!*abort_flag) mbar_wait_drain(bar(BAR_KV_EMPTY + s), last);
+      if (lane == 0) {
+        mbar_wait_drain(bar(BAR_Q), 0);
+        for (int s = 0; s < kKvStages && s < issued; ++s) {
+          const int last_idx = s + kKvStages * ((issued - 1 - s) / kKvStages);
+          const uint32_t last = (last_idx / kKvStages) & 1;
+          mbar_wait_drain(bar(BAR_KV_FULL + s), last);
+          if (!*abort_flag) mbar_wait_drain(bar(BAR_KV_EMPTY + s), last);
+        }
       }
     } else if (warp == 1 && lane == 0 && n_tiles > 0) {
       // ---------------------------------------------------------- MMA issuer

@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -374,6 +375,40 @@ int b200_rope_kv_write(const B200RopeParams* p, void* stream) {
                       ((p->cos_sin_stride_t * cse) & 15) == 0 &&
                       (p->is_neox ? (p->rotary_dim % 16 == 0) : (p->rotary_dim % 8 == 0));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nc = p->is_neox ? p->rotary_dim / 16 : p->rotary_dim / 8;  // rotation units per head
+  if (vec_ok && (nc == 4 || nc == 8 || nc == 16)) {
+    // Warp per token, grid-stride: exactly the CTAs that fit on the GPU at
+    // once (no partial second wave), or fewer when there are few tokens.
+    const int64_t warps_per_cta = b200::kRopeThreads / 32;
+    auto launch = [&](auto kernel) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, b200::kRopeThreads, 0) != cudaSuccess || per_sm <= 0)
+        per_sm = 1;
+      const int64_t resident = (int64_t)sm_count() * per_sm;
+      const int64_t needed = (p->num_tokens + warps_per_cta - 1) / warps_per_cta;
+      const dim3 grid((unsigned)std::max<int64_t>(1, std::min(resident, needed)));
+      kernel<<<grid, b200::kRopeThreads, 0, s>>>(a);
+    };
+#define B200_ROPE_WARP_NC(T, CS, NEOX)                                       \
+  switch (nc) {                                                              \
+    case 4: launch(b200::rope_kv_warp_kernel<T, CS, NEOX, 4>); break;        \
+    case 8: launch(b200::rope_kv_warp_kernel<T, CS, NEOX, 8>); break;        \
+    default: launch(b200::rope_kv_warp_kernel<T, CS, NEOX, 16>); break;      \
+  }
+#define B200_ROPE_WARP(T, CS)                   \
+  if (p->is_neox) { B200_ROPE_WARP_NC(T, CS, true) } else { B200_ROPE_WARP_NC(T, CS, false) }
+#define B200_ROPE_WARP_CS(T)                                                  \
+  switch (p->cos_sin_dtype) {                                                 \
+    case B200_DTYPE_BF16: B200_ROPE_WARP(T, __nv_bfloat16) break;             \
+    case B200_DTYPE_F16: B200_ROPE_WARP(T, __half) break;                     \
+    default: B200_ROPE_WARP(T, float) break;                                  \
+  }
+    if (p->dtype == B200_DTYPE_BF16) { B200_ROPE_WARP_CS(__nv_bfloat16) } else { B200_ROPE_WARP_CS(__half) }
+#undef B200_ROPE_WARP_CS
+#undef B200_ROPE_WARP
+#undef B200_ROPE_WARP_NC
+    return check_launch("rope_kv_warp_kernel");
+  }
   if (vec_ok) {
     const int half = p->rotary_dim / 2;
     const int n_rot = p->is_neox ? half / 8 : p->rotary_dim / 8;

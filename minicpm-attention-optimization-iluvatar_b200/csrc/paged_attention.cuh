@@ -405,15 +405,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               if (col < lo || col >= hi) sr[c4][c] = __float_as_uint(-INFINITY);
             }
         }
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        // Row maximum: eight independent chains of three-input max.
+        float mx[8];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          mx0 = fmaxf(mx0, __uint_as_float(sr[0][c]));
-          mx1 = fmaxf(mx1, __uint_as_float(sr[1][c]));
-          mx2 = fmaxf(mx2, __uint_as_float(sr[2][c]));
-          mx3 = fmaxf(mx3, __uint_as_float(sr[3][c]));
-        }
-        const float m_cand = fmaxf(m_used, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2);
+        for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              mx[k] = fmax3(mx[k], __uint_as_float(sr[c4][16 * h + 2 * k]), __uint_as_float(sr[c4][16 * h + 2 * k + 1]));
+        const float mxa = fmax3(mx[0], mx[1], mx[2]), mxb = fmax3(mx[3], mx[4], mx[5]);
+        const float m_cand = fmaxf(m_used, fmax3(mxa, mxb, fmaxf(mx[6], mx[7])) * sl2);
         const bool raise = m_cand > m_used + kRescaleThreshold;  // false while both are -inf
         if (__any_sync(0xffffffffu, raise)) {
           const float alpha = raise ? ex2_approx(m_used - m_cand) : 1.f;  // 0 when m_used = -inf
@@ -443,26 +447,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
         // P over the first 64 columns of S_t (column c = keys 2c, 2c+1), stored
         // 16 columns at a time as it is produced; S is already in registers.
-        float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
+        // Scale-and-subtract and the row sum run as f32x2 pairs (half the issue
+        // slots); exp2 on the special-function unit.
+        const uint64_t sl2_2 = f2_pack(sl2, sl2), negm_2 = f2_pack(neg_m, neg_m);
+        uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t pk[16];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c4][c]), sl2, neg_m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c4][c + 1]), sl2, neg_m));
-            if (c & 2) {
-              sum2 += p0;
-              sum3 += p1;
-            } else {
-              sum0 += p0;
-              sum1 += p1;
-            }
-            pk[c / 2] = Pack2<T>::pack(p0, p1);
+          for (int i = 0; i < 16; ++i) {
+            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[c4][2 * i]), __uint_as_float(sr[c4][2 * i + 1])), sl2_2, negm_2);
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+            if (i & 1) sum_b = f2_add(sum_b, f2_pack(p0, p1)); else sum_a = f2_add(sum_a, f2_pack(p0, p1));
+            pk[i] = Pack2<T>::pack(p0, p1);
           }
           tmem_st16(s_addr + 16 * c4, pk);
         }
-        l += (sum0 + sum1) + (sum2 + sum3);
+        {
+          float a0, a1;
+          f2_unpack(f2_add(sum_a, sum_b), a0, a1);
+          l += a0 + a1;
+        }
         if (t == 0 && j == n_tiles - 1 && v_tail_from < v_tail_to) {
           // Rows of the last page past the sequence end may hold anything (NaN
           // included); P is 0 there but 0 * NaN is NaN, so zero those V rows,

@@ -252,4 +252,143 @@ __global__ void __launch_bounds__(kRopeThreads) rope_kv_scalar_kernel(const Rope
   crow[d * a.c_sd] = vrow[d * a.v_sd];
 }
 
+// Warp-per-token path for the common shapes: lane l owns rotation unit
+// c = l % NC of every head (NC units per head, 32 % NC == 0), so it loads its
+// cos/sin chunk once per token and reuses it for all query and key heads.
+// The loads that do not depend on the position (a batch of query heads, the
+// key and value rows) are issued before the cos/sin row, and the next
+// token's position and slot are fetched a token ahead.
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  load8<T>(reinterpret_cast<const T*>(&u), v);
+}
+
+template <typename T, typename CS, bool NEOX, int NC>
+__global__ void __launch_bounds__(kRopeThreads, 2) rope_kv_warp_kernel(const RopeArgs a) {
+  constexpr int kHeadStep = 32 / NC;
+  // Query heads per lane whose loads are in flight together: eight 16-byte
+  // loads per lane either way (NeoX units span two chunks).
+  constexpr int kQBatch = NEOX ? 4 : 8;
+  const int lane = threadIdx.x & 31;
+  const int c = lane % NC, hg = lane / NC;
+  const int half = a.rd / 2;
+  const int n_pass = (a.head_dim - a.rd) / 8;
+  const int n_v = a.head_dim / 8;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  int64_t token = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  // The next token's position and slot are fetched one iteration ahead.
+  int64_t pos_n = 0, slot_n = -1;
+  if (token < a.num_tokens) {
+    pos_n = load_i(a.pos, token, a.pos_i64);
+    slot_n = load_i(a.slot, token, a.slot_i64);
+  }
+  for (; token < a.num_tokens; token += nwarps) {
+    const int64_t pos = pos_n, slot = slot_n;
+    if (token + nwarps < a.num_tokens) {
+      pos_n = load_i(a.pos, token + nwarps, a.pos_i64);
+      slot_n = load_i(a.slot, token + nwarps, a.slot_i64);
+    }
+    T* qtok = static_cast<T*>(a.q) + token * a.q_st;
+    const T* ktok = static_cast<const T*>(a.k) + token * a.k_st;
+    const T* vtok = static_cast<const T*>(a.v) + token * a.v_st;
+    // Issue this token's loads that do not depend on the position first.
+    uint4 q1[kQBatch], q2[kQBatch], k1, k2, vv;
+#pragma unroll
+    for (int k = 0; k < kQBatch; ++k) {
+      const int h = hg + k * kHeadStep;
+      if (h < a.hq) {
+        q1[k] = *reinterpret_cast<const uint4*>(qtok + h * a.q_sh + 8 * c);
+        if (NEOX) q2[k] = *reinterpret_cast<const uint4*>(qtok + h * a.q_sh + half + 8 * c);
+      }
+    }
+    const bool k_lane = hg < a.hkv;
+    if (k_lane) {
+      k1 = *reinterpret_cast<const uint4*>(ktok + hg * a.k_sh + 8 * c);
+      if (NEOX) k2 = *reinterpret_cast<const uint4*>(ktok + hg * a.k_sh + half + 8 * c);
+    }
+    const bool v_lane = lane < a.hkv * n_v;
+    if (v_lane) vv = *reinterpret_cast<const uint4*>(vtok + (lane / n_v) * a.v_sh + 8 * (lane % n_v));
+
+    if (pos < 0 || pos >= a.max_position) {
+      if (lane == 0) record_device_error(B200_DEVERR_POS_RANGE);
+      continue;
+    }
+    const CS* cs_row = static_cast<const CS*>(a.cs) + pos * a.cs_st;
+    float cv[8], sv[8];
+    if (NEOX) {
+      load8<CS>(cs_row + 8 * c, cv);
+      load8<CS>(cs_row + half + 8 * c, sv);
+    } else {
+      float c4[4], s4[4];
+      load4<CS>(cs_row + 4 * c, c4);
+      load4<CS>(cs_row + half + 4 * c, s4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        cv[i] = c4[i];
+        sv[i] = s4[i];
+      }
+    }
+    auto rotate_store = [&](const uint4& x1, const uint4& x2, T* row) {
+      float v1[8], y1[8];
+      unpack8<T>(x1, v1);
+      if (NEOX) {
+        float v2[8], y2[8];
+        unpack8<T>(x2, v2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rotate_pair(v1[i], v2[i], cv[i], sv[i], y1[i], y2[i]);
+        store8<T>(row + 8 * c, y1);
+        store8<T>(row + half + 8 * c, y2);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rotate_pair(v1[2 * i], v1[2 * i + 1], cv[i], sv[i], y1[2 * i], y1[2 * i + 1]);
+        store8<T>(row + 8 * c, y1);
+      }
+    };
+#pragma unroll
+    for (int k = 0; k < kQBatch; ++k) {
+      const int h = hg + k * kHeadStep;
+      if (h < a.hq) rotate_store(q1[k], q2[k], qtok + h * a.q_sh);
+    }
+    // Query heads beyond the first batch, a batch of loads at a time.
+    for (int h0 = hg + kQBatch * kHeadStep; h0 < a.hq; h0 += kQBatch * kHeadStep) {
+#pragma unroll
+      for (int k = 0; k < kQBatch; ++k) {
+        const int h = h0 + k * kHeadStep;
+        if (h < a.hq) {
+          q1[k] = *reinterpret_cast<const uint4*>(qtok + h * a.q_sh + 8 * c);
+          if (NEOX) q2[k] = *reinterpret_cast<const uint4*>(qtok + h * a.q_sh + half + 8 * c);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kQBatch; ++k) {
+        const int h = h0 + k * kHeadStep;
+        if (h < a.hq) rotate_store(q1[k], q2[k], qtok + h * a.q_sh);
+      }
+    }
+    if (slot < 0) continue;
+    if (slot >= a.num_slots) {
+      if (lane == 0) record_device_error(B200_DEVERR_SLOT_RANGE);
+      continue;
+    }
+    const int64_t blk = slot / a.block_size, off = slot - blk * a.block_size;
+    T* kc_tok = static_cast<T*>(a.kc) + blk * a.c_sb + off * a.c_st;
+    T* vc_tok = static_cast<T*>(a.vc) + blk * a.c_sb + off * a.c_st;
+    if (k_lane) rotate_store(k1, k2, kc_tok + hg * a.c_sh);
+    for (int h = hg + kHeadStep; h < a.hkv; h += kHeadStep) {
+      const uint4 x1 = *reinterpret_cast<const uint4*>(ktok + h * a.k_sh + 8 * c);
+      const uint4 x2 = NEOX ? *reinterpret_cast<const uint4*>(ktok + h * a.k_sh + half + 8 * c) : x1;
+      rotate_store(x1, x2, kc_tok + h * a.c_sh);
+    }
+    for (int i = lane; i < a.hkv * n_pass; i += 32) {
+      const int h = i / n_pass, d = a.rd + 8 * (i - h * n_pass);
+      *reinterpret_cast<uint4*>(kc_tok + h * a.c_sh + d) = *reinterpret_cast<const uint4*>(ktok + h * a.k_sh + d);
+    }
+    if (v_lane) *reinterpret_cast<uint4*>(vc_tok + (lane / n_v) * a.c_sh + 8 * (lane % n_v)) = vv;
+    for (int i = lane + 32; i < a.hkv * n_v; i += 32) {
+      const int h = i / n_v, d = 8 * (i - h * n_v);
+      *reinterpret_cast<uint4*>(vc_tok + h * a.c_sh + d) = *reinterpret_cast<const uint4*>(vtok + h * a.v_sh + d);
+    }
+  }
+}
+
 }  // namespace b200

@@ -272,15 +272,16 @@ def build_rope_batch(
 def rope_algorithmic_bytes(b: RopeBatch) -> int:
     """Bytes the RoPE + cache write must move at minimum.
 
-    Q read + write, K and V read, K and V cache rows written, one cos/sin row
-    read per token, positions and slots read.  Tokens with ``slot < 0`` move no
-    cache bytes.
+    The rotated part of Q read + written (Q's dims past ``rotary_dim`` are
+    left in place and need not move), K and V read, K and V cache rows written,
+    one cos/sin row read per token, positions and slots read.  Tokens with
+    ``slot < 0`` move no cache bytes.
     """
     t, hq, d = b.query.shape
     hkv = b.key.shape[1]
     e = b.query.element_size()
     written = int((b.slot_mapping >= 0).sum())
-    q_bytes = 2 * t * hq * d * e
+    q_bytes = 2 * t * hq * b.rotary_dim * e
     kv_read = 2 * t * hkv * d * e
     kv_write = 2 * written * hkv * d * e
     cs = t * b.rotary_dim * b.cos_sin_cache.element_size()

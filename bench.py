@@ -306,6 +306,40 @@ def rope_bench(args, world, rank, local):
         }), flush=True)
 
 
+# --------------------------------------------------------------------- verification
+def verify_sharded(args, batch, out, world, rank, splits):
+    """Gather every rank's rows on rank 0 (NCCL) and compare them with one
+    single-GPU call over the whole batch: a sequence's output does not depend
+    on which rank or which physical pages hold it, so they must match bit for
+    bit."""
+    import torch.distributed as dist
+
+    from minicpm_b200 import paged_split_kv_attention, workloads
+    from minicpm_b200.sharding import gather_rows_to_rank0
+
+    full = gather_rows_to_rank0(out, world, rank)
+    ids = [None] * world
+    if world > 1:
+        dist.all_gather_object(ids, list(batch.seq_ids))
+    else:
+        ids = [list(batch.seq_ids)]
+    if rank != 0:
+        return
+    order = [i for part in ids for i in part]
+    q, kv = workloads.WORKLOADS[args.workload]()
+    if args.num_seqs:
+        q, kv = q[: args.num_seqs], kv[: args.num_seqs]
+    ref = workloads.build_attention_batch([q[i] for i in order], [kv[i] for i in order], seq_ids=order).to(full.device)
+    want = torch.empty_like(ref.q)
+    paged_split_kv_attention(ref.q, ref.kv_cache[:, 0], ref.kv_cache[:, 1], want, ref.block_table, ref.seqused_k,
+                             ref.cu_seqlens_q, ref.max_seqlen_q, ref.max_seqlen_k, ref.softmax_scale, num_splits=splits)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(full, want))
+    print(json.dumps({"verify_rows": int(full.shape[0]), "verify_bit_identical": same}), flush=True)
+    if not same:
+        raise SystemExit("sharded output differs from the single-GPU output")
+
+
 # --------------------------------------------------------------------- attention bench
 def attention_bench(args, world, rank, local):
     from minicpm_b200 import iluvatar_attention, paged_split_kv_attention
@@ -393,11 +427,7 @@ def attention_bench(args, world, rank, local):
         assert torch.equal(host_out, out.cpu()), "e2e output differs from the device-resident run"
 
     if args.verify:
-        from minicpm_b200.sharding import gather_rows_to_rank0
-
-        full = gather_rows_to_rank0(out, world, rank)
-        if rank == 0:
-            print(json.dumps({"verify_rows": int(full.shape[0])}), flush=True)
+        verify_sharded(args, batch, out, world, rank, splits)
 
     if rank != 0:
         return

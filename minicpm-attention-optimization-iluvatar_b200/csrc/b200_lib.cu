@@ -14,12 +14,14 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <algorithm>
 #include <cstring>
 #include <mutex>
 
 #include "minicpm_b200.h"
 #include "paged_attention.cuh"
+#include "paged_attention_pair.cuh"
 #include "rope_kv_cache.cuh"
 #include "split_combine.cuh"
 
@@ -106,6 +108,12 @@ WorkspaceLayout attn_workspace_layout(int64_t total_q, int num_seqs, int hq, int
     w.total = align_up(w.l_off + rows * sizeof(float), 256);
   }
   return w;
+}
+
+// B200_ATTN_CTA_PAIR=1 selects the CTA-pair attention kernel, 0 the single-CTA one.
+bool use_cta_pair() {
+  const char* e = getenv("B200_ATTN_CTA_PAIR");
+  return e && e[0] == '1';
 }
 
 int auto_splits(int32_t total_q, int32_t num_seqs, int32_t hq, int32_t hkv, int32_t max_seqlen_k, int num_sms) {
@@ -253,12 +261,15 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   }
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // CTA-pair kernel (M = 256 UMMA across two SMs) or single-CTA kernel.
+  const bool pair = use_cta_pair();
+  const int units_per_tile_group = pair ? b200::kPairTilesPerUnit : b200::kAttnTilesPerUnit;
   b200::SchedArgs sa{};
   sa.cu_q = p->cu_seqlens_q;
   sa.seqused = p->seqused_k;
   sa.len_i64 = p->seqlen_dtype == B200_DTYPE_I64;
   sa.num_seqs = p->num_seqs;
-  sa.pos_per_unit = ppt * b200::kAttnTilesPerUnit;
+  sa.pos_per_unit = ppt * units_per_tile_group;
   sa.num_kv_heads = p->num_kv_heads;
   sa.num_splits = splits;
   sa.capacity = w.capacity;
@@ -293,7 +304,11 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   a.num_splits = splits;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
-  const dim3 grid(static_cast<unsigned>(w.capacity));
+  // Upper bound on work units for this unit size; surplus CTAs exit at once.
+  const int64_t units_ub =
+      ((int64_t)p->total_q + sa.pos_per_unit - 1) / sa.pos_per_unit + p->num_seqs;
+  const int64_t ctas = units_ub * p->num_kv_heads * splits * (pair ? 2 : 1);
+  const dim3 grid(static_cast<unsigned>(ctas));
   auto launch = [&](auto kernel) -> int {
     // The kernel rebalances registers between warpgroups with setmaxnreg; the
     // split adds up only if every thread was launched with exactly
@@ -302,12 +317,18 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
     if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess || fa.numRegs != b200::kAttnLaunchRegs)
       return fail(B200_ERR_CUDA, "paged_attn_fwd_kernel built with %d registers per thread, %d expected", fa.numRegs,
                   b200::kAttnLaunchRegs);
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kAttnSmemAlloc);
-    kernel<<<grid, b200::kAttnThreads, b200::kAttnSmemAlloc, s>>>(tm_q, tm_k, tm_v, a);
+    const uint32_t smem = pair ? b200::kAttnPairSmemAlloc : b200::kAttnSmemAlloc;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kernel<<<grid, b200::kAttnThreads, smem, s>>>(tm_q, tm_k, tm_v, a);
     return B200_OK;
   };
-  const int lr = (p->dtype == B200_DTYPE_BF16) ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16>)
-                                               : launch(b200::paged_attn_fwd_kernel<__half>);
+  int lr;
+  if (pair)
+    lr = (p->dtype == B200_DTYPE_BF16) ? launch(b200::paged_attn_fwd_pair_kernel<__nv_bfloat16>)
+                                       : launch(b200::paged_attn_fwd_pair_kernel<__half>);
+  else
+    lr = (p->dtype == B200_DTYPE_BF16) ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16>)
+                                       : launch(b200::paged_attn_fwd_kernel<__half>);
   if (lr != B200_OK) return lr;
   if (int r = check_launch("paged_attn_fwd_kernel")) return r;
 

@@ -76,8 +76,8 @@ enum : int {
   BAR_KV_FULL = 1,                           // + slot
   BAR_KV_EMPTY = BAR_KV_FULL + kKvStages,    // + slot
   BAR_S_FULL = BAR_KV_EMPTY + kKvStages,     // + tile
-  BAR_P_FULL = BAR_S_FULL + 2,               // + tile
-  BAR_O_DONE = BAR_P_FULL + 2,               // + tile
+  BAR_P_FULL = BAR_S_FULL + 2,               // + 4 * tile + quarter (32 keys of P)
+  BAR_O_DONE = BAR_P_FULL + 8,               // + tile
   BAR_DRAIN = BAR_O_DONE + 2,
   BAR_COUNT = BAR_DRAIN + 1
 };
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(BAR_S_FULL + t), 1);
-      mbar_init(bar(BAR_P_FULL + t), 4);
+      for (int q = 0; q < 4; ++q) mbar_init(bar(BAR_P_FULL + 4 * t + q), 4);
       mbar_init(bar(BAR_O_DONE + t), 1);
     }
     mbar_init(bar(BAR_DRAIN), 1);
@@ -310,13 +310,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         tc_commit(bar(BAR_S_FULL + t));
       };
-      auto issue_pv = [&](int t, uint32_t vslot_addr, bool acc) {
+      // O_t += P_t V, a quarter (32 keys, two K16 steps) at a time as the
+      // softmax warpgroup publishes each quarter of P.
+      auto issue_pv = [&](int t, int j, uint32_t vslot_addr, bool acc) {
+        for (int q = 0; q < 4; ++q) {
+          if (!mbar_wait(bar(BAR_P_FULL + 4 * t + q), j & 1, abort_flag)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, umma_desc_sw128(vslot_addr + kk * 2048, 16384, 1024),
-                  idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          for (int h = 0; h < 2; ++h) {
+            const int kk = 2 * q + h;
+            umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, umma_desc_sw128(vslot_addr + kk * 2048, 16384, 1024),
+                    idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          }
         }
         tc_commit(bar(BAR_O_DONE + t));
+        return true;
       };
       auto slot_addr = [&](int idx) { return sbase + kSmKV + (idx % kKvStages) * 32768; };
       auto wait_full = [&](int idx) {
@@ -333,18 +341,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int vidx = 2 * j + 1, kidx = 2 * j + 2;
         const bool more = j + 1 < n_tiles;
-        if (!wait_full(vidx) || !mbar_wait(bar(BAR_P_FULL + 0), j & 1, abort_flag)) break;
-        tc_fence_after();
-        issue_pv(0, slot_addr(vidx), j > 0);
+        if (!wait_full(vidx) || !issue_pv(0, j, slot_addr(vidx), j > 0)) break;
         if (more) {
           if (!wait_full(kidx)) break;
           tc_fence_after();
           issue_s(0, slot_addr(kidx));
         }
         if (two) {
-          if (!mbar_wait(bar(BAR_P_FULL + 1), j & 1, abort_flag)) break;
-          tc_fence_after();
-          issue_pv(1, slot_addr(vidx), j > 0);
+          if (!issue_pv(1, j, slot_addr(vidx), j > 0)) break;
           if (more) issue_s(1, slot_addr(kidx));
         }
         tc_commit(bar(BAR_KV_EMPTY + vidx % kKvStages));
@@ -444,11 +448,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
+        if (t == 0 && j == n_tiles - 1 && v_tail_from < v_tail_to) {
+          // Rows of the last page past the sequence end may hold anything (NaN
+          // included); P is 0 there but 0 * NaN is NaN, so zero those V rows,
+          // as the reference's masked V load does (triton_split_kv_paged.py:122).
+          // Done before the first quarter of P is published.
+          const int vidx = 2 * j + 1;
+          if (!mbar_wait(bar(BAR_KV_FULL + vidx % kKvStages), (vidx / kKvStages) & 1, abort_flag)) {
+            aborted = true;
+            break;
+          }
+          const uint32_t vbase = sbase + kSmKV + (vidx % kKvStages) * 32768;
+          const int n16 = (v_tail_to - v_tail_from) * 16;  // 16-byte pieces over both halves
+          for (int i = threadIdx.x - 128; i < n16; i += 128) {
+            const int r = v_tail_from + (i >> 4);
+            const int half = (i >> 3) & 1;
+            st_shared_v4(vbase + half * 16384 + r * 128 + (i & 7) * 16, 0u, 0u, 0u, 0u);
+          }
+          fence_proxy_async_smem();
+        }
 
         // P over the first 64 columns of S_t (column c = keys 2c, 2c+1), stored
-        // 16 columns at a time as it is produced; S is already in registers.
-        // Scale-and-subtract and the row sum run as f32x2 pairs (half the issue
-        // slots); exp2 on the special-function unit.
+        // and published a quarter (32 keys) at a time so that the PV UMMAs of
+        // this tile run while the rest of P is computed; S is already in
+        // registers.  Scale-and-subtract and the row sum run as f32x2 pairs
+        // (half the issue slots); exp2 on the special-function unit.
         const uint64_t sl2_2 = f2_pack(sl2, sl2), negm_2 = f2_pack(neg_m, neg_m);
         uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
 #pragma unroll
@@ -464,34 +488,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             pk[i] = Pack2<T>::pack(p0, p1);
           }
           tmem_st16(s_addr + 16 * c4, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(BAR_P_FULL + 4 * t + c4));  // one arrival per softmax warp
         }
         {
           float a0, a1;
           f2_unpack(f2_add(sum_a, sum_b), a0, a1);
           l += a0 + a1;
         }
-        if (t == 0 && j == n_tiles - 1 && v_tail_from < v_tail_to) {
-          // Rows of the last page past the sequence end may hold anything (NaN
-          // included); P is 0 there but 0 * NaN is NaN, so zero those V rows,
-          // as the reference's masked V load does (triton_split_kv_paged.py:122).
-          const int vidx = 2 * j + 1;
-          if (!mbar_wait(bar(BAR_KV_FULL + vidx % kKvStages), (vidx / kKvStages) & 1, abort_flag)) {
-            aborted = true;
-            break;
-          }
-          const uint32_t vbase = sbase + kSmKV + (vidx % kKvStages) * 32768;
-          const int n16 = (v_tail_to - v_tail_from) * 16;  // 16-byte pieces over both halves
-          for (int i = threadIdx.x - 128; i < n16; i += 128) {
-            const int r = v_tail_from + (i >> 4);
-            const int half = (i >> 3) & 1;
-            st_shared_v4(vbase + half * 16384 + r * 128 + (i & 7) * 16, 0u, 0u, 0u, 0u);
-          }
-          fence_proxy_async_smem();
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(BAR_P_FULL + t));  // one arrival per softmax warp
       }
 
       // ---------------------------------------------------------- epilogue

@@ -27,6 +27,15 @@
  *                             (the reference has no automatic choice).
  *   b200_attn_workspace_bytes -> the per-call scratch allocation of
  *                             kernels/triton_split_kv_paged.py:295-306.
+ *   b200_kv_cache_write    -> the service's plain KV-cache update,
+ *                             IluvatarAttentionImpl.do_kv_cache_update
+ *                             (integration/vllm-plugin-FL-split-kv.patch:815-858),
+ *                             i.e. vLLM's triton_reshape_and_cache_flash and
+ *                             triton_reshape_and_cache_flash_per_token_head_quant.
+ *   b200_rope_kv_write with key_out / an fp8 cache
+ *                          -> the service RoPE ABI,
+ *                             IluvatarAttentionImpl.do_rope_and_kv_cache_update
+ *                             (integration/vllm-plugin-FL-split-kv.patch:865-899).
  */
 #ifndef MINICPM_B200_H_
 #define MINICPM_B200_H_
@@ -38,7 +47,7 @@
 extern "C" {
 #endif
 
-#define B200_ABI_VERSION 1
+#define B200_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define B200_API __attribute__((visibility("default")))
@@ -59,6 +68,15 @@ extern "C" {
 #define B200_DTYPE_F32 2
 #define B200_DTYPE_I32 3
 #define B200_DTYPE_I64 4
+#define B200_DTYPE_FP8_E4M3 5 /* cache element types of the quantised KV-cache writes */
+#define B200_DTYPE_FP8_E5M2 6
+#define B200_DTYPE_I8 7
+
+/* KV-cache quantisation modes (same numbering as vLLM's KVQuantMode). */
+#define B200_KVQ_NONE 0               /* cache dtype == key dtype: bit copy                */
+#define B200_KVQ_FP8_PER_TENSOR 1     /* fp8(x / scale), one device float per cache        */
+#define B200_KVQ_INT8_PER_TOKEN_HEAD 2 /* int8 with a dynamic scale per (token, head)      */
+#define B200_KVQ_FP8_PER_TOKEN_HEAD 3  /* fp8 e4m3 with a dynamic scale per (token, head)  */
 
 /* Device-side error codes (b200_device_error). */
 #define B200_DEVERR_NONE 0u
@@ -202,9 +220,66 @@ typedef struct B200RopeParams {
   int32_t cos_sin_dtype;  /* F16 / BF16 / F32 */
   int32_t position_dtype; /* I32 / I64 */
   int32_t slot_dtype;     /* I32 / I64 */
+  /* Service ABI (vLLM's rope-and-cache call with k_out = key):            */
+  void* key_out;          /* NULL: key untouched; else rotated key [T, Hkv, D] stored here
+                             for every token (may alias key)                             */
+  int64_t ko_stride_t, ko_stride_h;
+  int32_t cache_dtype;    /* == dtype, or FP8_E4M3 / FP8_E5M2: caches hold
+                             fp8(round_to_dtype(x) / scale), RNE, saturating             */
+  const float* k_scale;   /* fp8 caches: one device float each                           */
+  const float* v_scale;
 } B200RopeParams;
 
 B200_API int b200_rope_kv_write(const B200RopeParams* params, void* stream);
+
+/*
+ * Paged KV-cache write (vLLM "flash" layout): for every token t with
+ * slot_mapping[t] >= 0, key[t, h, :] -> key_cache[slot / bs, slot % bs, h, :]
+ * and value[t, h, :] -> value_cache[...], as
+ *   B200_KVQ_NONE                bit copy (cache_dtype == dtype);
+ *   B200_KVQ_FP8_PER_TENSOR      fp8(x / *k_scale) (resp. *v_scale), x / s rounded to
+ *                                nearest, fp8 round-to-nearest-even, saturating to the
+ *                                largest finite value;
+ *   B200_KVQ_*_PER_TOKEN_HEAD    s = max(max_d |x| / QMAX, 1e-6) per (token, head),
+ *                                q = clamp(x * (1 / s), QMIN, QMAX) -> int8 by truncation
+ *                                toward zero (QMAX 127, QMIN -128) or fp8 e4m3 RNE (±448);
+ *                                s stored to k_scale_cache / v_scale_cache
+ *                                [num_blocks, block_size, num_kv_heads] (float strides).
+ * key, value [num_tokens, num_kv_heads, head_dim] (F16 / BF16 / F32), d contiguous;
+ * caches [num_blocks, block_size, num_kv_heads, >= head_dim], d contiguous (the
+ * per-token-head caches may carry the scale inline after head_dim).  Slots
+ * >= num_blocks * block_size are skipped and recorded (B200_DEVERR_SLOT_RANGE).
+ * Alignment: key / value rows 16 bytes; cache rows 16 bytes (NONE), 4 bytes (1-byte types).
+ */
+typedef struct B200KvWriteParams {
+  const void* key;
+  const void* value;
+  void* key_cache;
+  void* value_cache;
+  const void* slot_mapping;
+  const float* k_scale;  /* FP8_PER_TENSOR */
+  const float* v_scale;
+  float* k_scale_cache;  /* *_PER_TOKEN_HEAD */
+  float* v_scale_cache;
+  int64_t k_stride_t, k_stride_h;
+  int64_t v_stride_t, v_stride_h;
+  int64_t kc_stride_block, kc_stride_tok, kc_stride_head;
+  int64_t vc_stride_block, vc_stride_tok, vc_stride_head;
+  int64_t ks_stride_block, ks_stride_tok, ks_stride_head;
+  int64_t vs_stride_block, vs_stride_tok, vs_stride_head;
+  int32_t num_tokens;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t block_size;
+  int32_t num_blocks;
+  int32_t dtype;       /* key / value: F16 / BF16 / F32 */
+  int32_t cache_dtype; /* NONE: == dtype; FP8_PER_TENSOR: FP8_E4M3 / FP8_E5M2;
+                          INT8_PER_TOKEN_HEAD: I8; FP8_PER_TOKEN_HEAD: FP8_E4M3 */
+  int32_t quant_mode;  /* B200_KVQ_* */
+  int32_t slot_dtype;  /* I32 / I64 */
+} B200KvWriteParams;
+
+B200_API int b200_kv_cache_write(const B200KvWriteParams* params, void* stream);
 
 /* Message of the last failed call on this host thread ("" if none). */
 B200_API const char* b200_last_error(void);

@@ -24,6 +24,7 @@
 #include "paged_attention_pair.cuh"
 #include "rope_kv_cache.cuh"
 #include "split_combine.cuh"
+#include "kv_cache_write.cuh"
 
 namespace {
 
@@ -371,6 +372,11 @@ int b200_rope_kv_write(const B200RopeParams* p, void* stream) {
       (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256) || p->block_size <= 0 || p->block_size % 16 ||
       p->num_kv_heads <= 0)
     return fail(B200_ERR_INVALID, "unsupported RoPE/cache shape");
+  const bool fp8_cache = p->cache_dtype == B200_DTYPE_FP8_E4M3 || p->cache_dtype == B200_DTYPE_FP8_E5M2;
+  if (p->cache_dtype != p->dtype && !fp8_cache)
+    return fail(B200_ERR_INVALID, "the caches must have the query dtype or be float8 e4m3 / e5m2");
+  if (fp8_cache && (!p->k_scale || !p->v_scale)) return fail(B200_ERR_INVALID, "fp8 caches need k_scale and v_scale");
+  const bool svc = fp8_cache || p->key_out != nullptr;
   if (p->num_tokens <= 0) return B200_OK;
 
   b200::RopeArgs a{};
@@ -386,18 +392,33 @@ int b200_rope_kv_write(const B200RopeParams* p, void* stream) {
   a.rd = p->rotary_dim; a.block_size = p->block_size; a.max_position = p->max_position;
   a.pos_i64 = p->position_dtype == B200_DTYPE_I64;
   a.slot_i64 = p->slot_dtype == B200_DTYPE_I64;
+  a.ko = p->key_out; a.ko_st = p->ko_stride_t; a.ko_sh = p->ko_stride_h;
+  a.cache_elem = p->cache_dtype == B200_DTYPE_FP8_E4M3 ? b200::kElemE4M3
+                 : p->cache_dtype == B200_DTYPE_FP8_E5M2 ? b200::kElemE5M2 : b200::kElemSame;
+  a.k_scale = p->k_scale; a.v_scale = p->v_scale;
 
   const int cse = p->cos_sin_dtype == B200_DTYPE_F32 ? 4 : 2;
-  const bool vec_ok = p->q_stride_d == 1 && p->k_stride_d == 1 && p->v_stride_d == 1 && p->cache_stride_d == 1 &&
-                      aligned16(p->query) && aligned16(p->key) && aligned16(p->value) && aligned16(p->key_cache) &&
-                      aligned16(p->value_cache) && aligned16(p->cos_sin_cache) &&
-                      (((p->q_stride_t | p->q_stride_h | p->k_stride_t | p->k_stride_h | p->v_stride_t | p->v_stride_h |
-                         p->cache_stride_block | p->cache_stride_tok | p->cache_stride_head) * 2) & 15) == 0 &&
+  // Cache rows: 16-byte aligned for the model dtype, 4-byte for fp8.
+  const int64_t ce = fp8_cache ? 1 : 2, calign = fp8_cache ? 4 : 16;
+  const bool cache_ok = p->cache_stride_d == 1 &&
+                        (reinterpret_cast<uintptr_t>(p->key_cache) | reinterpret_cast<uintptr_t>(p->value_cache)) %
+                                calign == 0 &&
+                        ((p->cache_stride_block | p->cache_stride_tok | p->cache_stride_head) * ce) % calign == 0;
+  const bool vec_ok = p->q_stride_d == 1 && p->k_stride_d == 1 && p->v_stride_d == 1 && cache_ok &&
+                      aligned16(p->query) && aligned16(p->key) && aligned16(p->value) && aligned16(p->cos_sin_cache) &&
+                      (((p->q_stride_t | p->q_stride_h | p->k_stride_t | p->k_stride_h | p->v_stride_t | p->v_stride_h) *
+                        2) & 15) == 0 &&
                       ((p->cos_sin_stride_t * cse) & 15) == 0 &&
+                      (!p->key_out || (aligned16(p->key_out) && (((p->ko_stride_t | p->ko_stride_h) * 2) & 15) == 0)) &&
                       (p->is_neox ? (p->rotary_dim % 16 == 0) : (p->rotary_dim % 8 == 0));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nc = p->is_neox ? p->rotary_dim / 16 : p->rotary_dim / 8;  // rotation units per head
-  if (vec_ok && (nc == 4 || nc == 8 || nc == 16)) {
+  const bool warp_ok = vec_ok && (nc == 4 || nc == 8 || nc == 16);
+  if (svc && !warp_ok)
+    return fail(B200_ERR_UNSUPPORTED,
+                "key_out / fp8 caches need 16-byte aligned rows with contiguous head_dim and rotary_dim "
+                "64, 128 or 256 (NeoX) or 32, 64 or 128 (interleaved)");
+  if (warp_ok) {
     // Warp per token, grid-stride: exactly the CTAs that fit on the GPU at
     // once (no partial second wave), or fewer when there are few tokens.
     const int64_t warps_per_cta = b200::kRopeThreads / 32;
@@ -410,11 +431,14 @@ int b200_rope_kv_write(const B200RopeParams* p, void* stream) {
       const dim3 grid((unsigned)std::max<int64_t>(1, std::min(resident, needed)));
       kernel<<<grid, b200::kRopeThreads, 0, s>>>(a);
     };
+#define B200_ROPE_WARP_SVC(T, CS, NEOX, NC)                                        \
+  if (svc) launch(b200::rope_kv_warp_kernel<T, CS, NEOX, NC, true>);               \
+  else launch(b200::rope_kv_warp_kernel<T, CS, NEOX, NC, false>);
 #define B200_ROPE_WARP_NC(T, CS, NEOX)                                       \
   switch (nc) {                                                              \
-    case 4: launch(b200::rope_kv_warp_kernel<T, CS, NEOX, 4>); break;        \
-    case 8: launch(b200::rope_kv_warp_kernel<T, CS, NEOX, 8>); break;        \
-    default: launch(b200::rope_kv_warp_kernel<T, CS, NEOX, 16>); break;      \
+    case 4: B200_ROPE_WARP_SVC(T, CS, NEOX, 4) break;                        \
+    case 8: B200_ROPE_WARP_SVC(T, CS, NEOX, 8) break;                        \
+    default: B200_ROPE_WARP_SVC(T, CS, NEOX, 16) break;                      \
   }
 #define B200_ROPE_WARP(T, CS)                   \
   if (p->is_neox) { B200_ROPE_WARP_NC(T, CS, true) } else { B200_ROPE_WARP_NC(T, CS, false) }
@@ -428,6 +452,7 @@ int b200_rope_kv_write(const B200RopeParams* p, void* stream) {
 #undef B200_ROPE_WARP_CS
 #undef B200_ROPE_WARP
 #undef B200_ROPE_WARP_NC
+#undef B200_ROPE_WARP_SVC
     return check_launch("rope_kv_warp_kernel");
   }
   if (vec_ok) {
@@ -467,6 +492,90 @@ int b200_rope_kv_write(const B200RopeParams* p, void* stream) {
 #undef B200_ROPE_SCS
 #undef B200_ROPE_SC
   return check_launch("rope_kv_scalar_kernel");
+}
+
+int b200_kv_cache_write(const B200KvWriteParams* p, void* stream) {
+  if (!p) return fail(B200_ERR_INVALID, "null params");
+  if (p->dtype != B200_DTYPE_BF16 && p->dtype != B200_DTYPE_F16 && p->dtype != B200_DTYPE_F32)
+    return fail(B200_ERR_INVALID, "key/value must be f16, bf16 or f32");
+  if (p->slot_dtype != B200_DTYPE_I32 && p->slot_dtype != B200_DTYPE_I64)
+    return fail(B200_ERR_INVALID, "slot_mapping must contain int32 or int64 indices");
+  if ((p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256) || p->num_kv_heads <= 0 || p->block_size <= 0 ||
+      p->num_blocks < 0)
+    return fail(B200_ERR_INVALID, "unsupported KV-cache shape (head_dim must be 64, 128 or 256)");
+  int elem = b200::kElemSame;
+  switch (p->quant_mode) {
+    case B200_KVQ_NONE:
+      if (p->cache_dtype != p->dtype) return fail(B200_ERR_INVALID, "an unquantised cache must have the key dtype");
+      break;
+    case B200_KVQ_FP8_PER_TENSOR:
+      if (p->cache_dtype != B200_DTYPE_FP8_E4M3 && p->cache_dtype != B200_DTYPE_FP8_E5M2)
+        return fail(B200_ERR_INVALID, "fp8 per-tensor caches must be float8 e4m3 or e5m2");
+      if (!p->k_scale || !p->v_scale) return fail(B200_ERR_INVALID, "fp8 per-tensor caches need k_scale and v_scale");
+      elem = p->cache_dtype == B200_DTYPE_FP8_E4M3 ? b200::kElemE4M3 : b200::kElemE5M2;
+      break;
+    case B200_KVQ_INT8_PER_TOKEN_HEAD:
+    case B200_KVQ_FP8_PER_TOKEN_HEAD: {
+      const int want = p->quant_mode == B200_KVQ_INT8_PER_TOKEN_HEAD ? B200_DTYPE_I8 : B200_DTYPE_FP8_E4M3;
+      if (p->cache_dtype != want)
+        return fail(B200_ERR_INVALID, "per-token-head caches must be int8 (int8 mode) or float8 e4m3 (fp8 mode)");
+      if (!p->k_scale_cache || !p->v_scale_cache)
+        return fail(B200_ERR_INVALID, "per-token-head caches need k_scale_cache and v_scale_cache");
+      elem = p->quant_mode == B200_KVQ_INT8_PER_TOKEN_HEAD ? b200::kElemI8 : b200::kElemE4M3;
+      break;
+    }
+    default:
+      return fail(B200_ERR_UNSUPPORTED, "KV quantisation mode %d is not supported", p->quant_mode);
+  }
+  if (p->num_tokens <= 0) return B200_OK;
+  const int64_t ie = p->dtype == B200_DTYPE_F32 ? 4 : 2;
+  if (!aligned16(p->key) || !aligned16(p->value) ||
+      ((p->k_stride_t | p->k_stride_h | p->v_stride_t | p->v_stride_h) * ie) & 15)
+    return fail(B200_ERR_UNSUPPORTED, "key/value rows must be 16-byte aligned with contiguous head_dim");
+  const int64_t ce = p->quant_mode == B200_KVQ_NONE ? ie : 1;
+  const int64_t calign = p->quant_mode == B200_KVQ_NONE ? 16 : 4;
+  if ((reinterpret_cast<uintptr_t>(p->key_cache) | reinterpret_cast<uintptr_t>(p->value_cache)) % calign ||
+      ((p->kc_stride_block | p->kc_stride_tok | p->kc_stride_head | p->vc_stride_block | p->vc_stride_tok |
+        p->vc_stride_head) * ce) % calign)
+    return fail(B200_ERR_UNSUPPORTED, "cache rows must be %d-byte aligned with contiguous head_dim", (int)calign);
+
+  b200::KvWriteArgs a{};
+  a.k = p->key; a.v = p->value; a.kc = p->key_cache; a.vc = p->value_cache; a.slot = p->slot_mapping;
+  a.k_scale = p->k_scale; a.v_scale = p->v_scale; a.ksc = p->k_scale_cache; a.vsc = p->v_scale_cache;
+  a.k_st = p->k_stride_t; a.k_sh = p->k_stride_h; a.v_st = p->v_stride_t; a.v_sh = p->v_stride_h;
+  a.kc_sb = p->kc_stride_block; a.kc_st = p->kc_stride_tok; a.kc_sh = p->kc_stride_head;
+  a.vc_sb = p->vc_stride_block; a.vc_st = p->vc_stride_tok; a.vc_sh = p->vc_stride_head;
+  a.ks_sb = p->ks_stride_block; a.ks_st = p->ks_stride_tok; a.ks_sh = p->ks_stride_head;
+  a.vs_sb = p->vs_stride_block; a.vs_st = p->vs_stride_tok; a.vs_sh = p->vs_stride_head;
+  a.num_slots = (int64_t)p->num_blocks * p->block_size;
+  a.num_tokens = p->num_tokens; a.hkv = p->num_kv_heads; a.head_dim = p->head_dim; a.block_size = p->block_size;
+  a.slot_i64 = p->slot_dtype == B200_DTYPE_I64;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto launch = [&](auto kernel) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, b200::kKvWriteThreads, 0) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 1;
+    const int64_t warps_per_cta = b200::kKvWriteThreads / 32;
+    const int64_t resident = (int64_t)sm_count() * per_sm;
+    const int64_t needed = (p->num_tokens + warps_per_cta - 1) / warps_per_cta;
+    kernel<<<dim3((unsigned)std::max<int64_t>(1, std::min(resident, needed))), b200::kKvWriteThreads, 0, s>>>(a);
+  };
+#define B200_KV_MODES(T)                                                                                  \
+  if (p->quant_mode == B200_KVQ_NONE) launch(b200::kv_cache_write_kernel<T, b200::kKvCopy, b200::kElemSame>); \
+  else if (p->quant_mode == B200_KVQ_FP8_PER_TENSOR) {                                                    \
+    if (elem == b200::kElemE4M3) launch(b200::kv_cache_write_kernel<T, b200::kKvFp8Tensor, b200::kElemE4M3>); \
+    else launch(b200::kv_cache_write_kernel<T, b200::kKvFp8Tensor, b200::kElemE5M2>);                       \
+  } else if (elem == b200::kElemI8) launch(b200::kv_cache_write_kernel<T, b200::kKvPerTokenHead, b200::kElemI8>); \
+  else launch(b200::kv_cache_write_kernel<T, b200::kKvPerTokenHead, b200::kElemE4M3>);
+  switch (p->dtype) {
+    case B200_DTYPE_BF16: B200_KV_MODES(__nv_bfloat16) break;
+    case B200_DTYPE_F16: B200_KV_MODES(__half) break;
+    default: B200_KV_MODES(float) break;
+  }
+#undef B200_KV_MODES
+  return check_launch("kv_cache_write_kernel");
 }
 
 int b200_device_error(void* stream, uint32_t* code) {

@@ -13,6 +13,14 @@
 // Out-of-range indices, which the reference would read or write out of
 // bounds, are skipped here and recorded in the device error word.
 //
+// The service variant (IluvatarAttentionImpl.do_rope_and_kv_cache_update,
+// integration/vllm-plugin-FL-split-kv.patch:865-899, which passes
+// k_out = key) additionally stores the rotated key of every token to key_out
+// and may write fp8 caches: the value the cache receives is the one an
+// unfused rotate-then-cache-update sequence would store, i.e. the rotated
+// element rounded to the model dtype, divided by k_scale / v_scale (rounded
+// to nearest) and converted to fp8 (RNE, saturating).
+//
 // Bandwidth kernel: one thread per 8-element unit (a NeoX unit is the chunk
 // at d plus its partner chunk at d + rd/2), 16-byte loads and stores.
 #pragma once
@@ -20,6 +28,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "kv_cache_write.cuh"
 #include "split_combine.cuh"
 
 namespace b200 {
@@ -43,6 +52,12 @@ struct RopeArgs {
   int64_t num_slots;
   int num_tokens, hq, hkv, head_dim, rd, block_size, max_position;
   int pos_i64, slot_i64;
+  // Service variant only.
+  void* ko;
+  int64_t ko_st, ko_sh;
+  int cache_elem;  // KvCacheElem: kElemSame, kElemE4M3 or kElemE5M2
+  const float* k_scale;
+  const float* v_scale;
 };
 
 __device__ __forceinline__ int64_t load_i(const void* p, int64_t i, int is_i64) {
@@ -263,7 +278,39 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
   load8<T>(reinterpret_cast<const T*>(&u), v);
 }
 
-template <typename T, typename CS, bool NEOX, int NC>
+// Eight rotated values (fp32) to a cache row: the model dtype, or fp8 of the
+// value rounded to the model dtype and divided by the cache's scale.
+template <typename T>
+__device__ __forceinline__ void cache_store8(void* base, int64_t off, const float (&y)[8], int elem, float scale) {
+  if (elem == kElemSame) {
+    store8<T>(static_cast<T*>(base) + off, y);
+    return;
+  }
+  float r[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) r[i] = to_f32<T>(from_f32<T>(y[i]));
+  uint8_t* p = static_cast<uint8_t*>(base) + off;
+  if (elem == kElemE4M3) store_fp8_scaled<kElemE4M3>(p, r, scale);
+  else store_fp8_scaled<kElemE5M2>(p, r, scale);
+}
+
+// Eight unrotated elements (raw) to a cache row.
+template <typename T>
+__device__ __forceinline__ void cache_copy8(void* base, int64_t off, const uint4& x, int elem, float scale) {
+  if (elem == kElemSame) {
+    *reinterpret_cast<uint4*>(static_cast<T*>(base) + off) = x;
+    return;
+  }
+  float v[8];
+  load8<T>(reinterpret_cast<const T*>(&x), v);
+  uint8_t* p = static_cast<uint8_t*>(base) + off;
+  if (elem == kElemE4M3) store_fp8_scaled<kElemE4M3>(p, v, scale);
+  else store_fp8_scaled<kElemE5M2>(p, v, scale);
+}
+
+// SVC = the service variant (key_out and / or an fp8 cache); SVC = false is
+// the reference operator's path.
+template <typename T, typename CS, bool NEOX, int NC, bool SVC>
 __global__ void __launch_bounds__(kRopeThreads, 2) rope_kv_warp_kernel(const RopeArgs a) {
   constexpr int kHeadStep = 32 / NC;
   // Query heads per lane whose loads are in flight together: eight 16-byte
@@ -364,6 +411,65 @@ __global__ void __launch_bounds__(kRopeThreads, 2) rope_kv_warp_kernel(const Rop
         const int h = h0 + k * kHeadStep;
         if (h < a.hq) rotate_store(q1[k], q2[k], qtok + h * a.q_sh);
       }
+    }
+    if (SVC) {
+      // Rotated key to key_out for every token; caches only for valid slots.
+      const bool in_range = slot >= 0 && slot < a.num_slots;
+      if (slot >= a.num_slots && lane == 0) record_device_error(B200_DEVERR_SLOT_RANGE);
+      int64_t ctok = 0;
+      if (in_range) {
+        const int64_t blk = slot / a.block_size;
+        ctok = blk * a.c_sb + (slot - blk * a.block_size) * a.c_st;
+      }
+      float ks = 1.0f, vs = 1.0f;
+      if (a.cache_elem != kElemSame) {
+        ks = *a.k_scale;
+        vs = *a.v_scale;
+      }
+      T* kotok = a.ko ? static_cast<T*>(a.ko) + token * a.ko_st : nullptr;
+      auto rotate_key = [&](const uint4& x1, const uint4& x2, int h) {
+        float v1[8], y1[8], y2[8];
+        unpack8<T>(x1, v1);
+        if (NEOX) {
+          float v2[8];
+          unpack8<T>(x2, v2);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rotate_pair(v1[i], v2[i], cv[i], sv[i], y1[i], y2[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) rotate_pair(v1[2 * i], v1[2 * i + 1], cv[i], sv[i], y1[2 * i], y1[2 * i + 1]);
+        }
+        if (kotok) {
+          store8<T>(kotok + h * a.ko_sh + 8 * c, y1);
+          if (NEOX) store8<T>(kotok + h * a.ko_sh + half + 8 * c, y2);
+        }
+        if (in_range) {
+          cache_store8<T>(a.kc, ctok + h * a.c_sh + 8 * c, y1, a.cache_elem, ks);
+          if (NEOX) cache_store8<T>(a.kc, ctok + h * a.c_sh + half + 8 * c, y2, a.cache_elem, ks);
+        }
+      };
+      if (k_lane) rotate_key(k1, k2, hg);
+      for (int h = hg + kHeadStep; h < a.hkv; h += kHeadStep) {
+        const uint4 x1 = *reinterpret_cast<const uint4*>(ktok + h * a.k_sh + 8 * c);
+        const uint4 x2 = NEOX ? *reinterpret_cast<const uint4*>(ktok + h * a.k_sh + half + 8 * c) : x1;
+        rotate_key(x1, x2, h);
+      }
+      const bool ko_copy = kotok && a.ko != a.k;  // pass-through dims of an in-place key_out stay as they are
+      for (int i = lane; i < a.hkv * n_pass; i += 32) {
+        const int h = i / n_pass, d = a.rd + 8 * (i - h * n_pass);
+        const uint4 x = *reinterpret_cast<const uint4*>(ktok + h * a.k_sh + d);
+        if (ko_copy) *reinterpret_cast<uint4*>(kotok + h * a.ko_sh + d) = x;
+        if (in_range) cache_copy8<T>(a.kc, ctok + h * a.c_sh + d, x, a.cache_elem, ks);
+      }
+      if (in_range) {
+        if (v_lane) cache_copy8<T>(a.vc, ctok + (lane / n_v) * a.c_sh + 8 * (lane % n_v), vv, a.cache_elem, vs);
+        for (int i = lane + 32; i < a.hkv * n_v; i += 32) {
+          const int h = i / n_v, d = 8 * (i - h * n_v);
+          cache_copy8<T>(a.vc, ctok + h * a.c_sh + d, *reinterpret_cast<const uint4*>(vtok + h * a.v_sh + d),
+                         a.cache_elem, vs);
+        }
+      }
+      continue;
     }
     if (slot < 0) continue;
     if (slot >= a.num_slots) {

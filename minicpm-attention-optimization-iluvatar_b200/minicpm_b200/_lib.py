@@ -27,6 +27,17 @@ DTYPE_BF16 = 1
 DTYPE_F32 = 2
 DTYPE_I32 = 3
 DTYPE_I64 = 4
+DTYPE_FP8_E4M3 = 5
+DTYPE_FP8_E5M2 = 6
+DTYPE_I8 = 7
+
+# KV-cache quantisation modes (numbering of vLLM's KVQuantMode).
+KVQ_NONE = 0
+KVQ_FP8_PER_TENSOR = 1
+KVQ_INT8_PER_TOKEN_HEAD = 2
+KVQ_FP8_PER_TOKEN_HEAD = 3
+
+ABI_VERSION = 2
 
 DEVERR_NONE = 0
 DEVERR_WAIT_TIMEOUT = 1
@@ -39,6 +50,9 @@ _TORCH_DTYPES = {
     torch.float32: DTYPE_F32,
     torch.int32: DTYPE_I32,
     torch.int64: DTYPE_I64,
+    torch.float8_e4m3fn: DTYPE_FP8_E4M3,
+    torch.float8_e5m2: DTYPE_FP8_E5M2,
+    torch.int8: DTYPE_I8,
 }
 
 EXPORTED_SYMBOLS = (
@@ -48,7 +62,9 @@ EXPORTED_SYMBOLS = (
     "b200_attn_workspace_bytes",
     "b200_paged_attn_fwd",
     "b200_split_combine",
+    "b200_paged_attn_fwd_noalloc",
     "b200_rope_kv_write",
+    "b200_kv_cache_write",
     "b200_device_error",
 )
 
@@ -99,6 +115,23 @@ class RopeParams(ctypes.Structure):
         ("num_tokens", i32), ("num_q_heads", i32), ("num_kv_heads", i32), ("head_dim", i32),
         ("rotary_dim", i32), ("block_size", i32), ("num_blocks", i32), ("max_position", i32),
         ("is_neox", i32), ("dtype", i32), ("cos_sin_dtype", i32), ("position_dtype", i32), ("slot_dtype", i32),
+        ("key_out", c_void_p), ("ko_stride_t", i64), ("ko_stride_h", i64),
+        ("cache_dtype", i32), ("k_scale", c_void_p), ("v_scale", c_void_p),
+    ]
+
+
+class KvWriteParams(ctypes.Structure):
+    _fields_ = [
+        ("key", c_void_p), ("value", c_void_p), ("key_cache", c_void_p), ("value_cache", c_void_p),
+        ("slot_mapping", c_void_p), ("k_scale", c_void_p), ("v_scale", c_void_p),
+        ("k_scale_cache", c_void_p), ("v_scale_cache", c_void_p),
+        ("k_stride_t", i64), ("k_stride_h", i64), ("v_stride_t", i64), ("v_stride_h", i64),
+        ("kc_stride_block", i64), ("kc_stride_tok", i64), ("kc_stride_head", i64),
+        ("vc_stride_block", i64), ("vc_stride_tok", i64), ("vc_stride_head", i64),
+        ("ks_stride_block", i64), ("ks_stride_tok", i64), ("ks_stride_head", i64),
+        ("vs_stride_block", i64), ("vs_stride_tok", i64), ("vs_stride_head", i64),
+        ("num_tokens", i32), ("num_kv_heads", i32), ("head_dim", i32), ("block_size", i32), ("num_blocks", i32),
+        ("dtype", i32), ("cache_dtype", i32), ("quant_mode", i32), ("slot_dtype", i32),
     ]
 
 
@@ -133,9 +166,13 @@ def load() -> ctypes.CDLL:
         lib.b200_split_combine.argtypes = [ctypes.POINTER(CombineParams), c_void_p]
         lib.b200_rope_kv_write.restype = ctypes.c_int
         lib.b200_rope_kv_write.argtypes = [ctypes.POINTER(RopeParams), c_void_p]
+        lib.b200_paged_attn_fwd_noalloc.restype = ctypes.c_int
+        lib.b200_paged_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnParams), c_void_p]
+        lib.b200_kv_cache_write.restype = ctypes.c_int
+        lib.b200_kv_cache_write.argtypes = [ctypes.POINTER(KvWriteParams), c_void_p]
         lib.b200_device_error.restype = ctypes.c_int
         lib.b200_device_error.argtypes = [c_void_p, ctypes.POINTER(ctypes.c_uint32)]
-        if lib.b200_abi_version() != 1:
+        if lib.b200_abi_version() != ABI_VERSION:
             raise RuntimeError("libminicpm_b200.so ABI version mismatch; rebuild it")
         _lib = lib
     return _lib

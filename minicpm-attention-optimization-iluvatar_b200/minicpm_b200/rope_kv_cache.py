@@ -110,6 +110,7 @@ def fused_rope_and_cache(
         max_position=cos_sin_cache.shape[0], is_neox=int(bool(is_neox)),
         dtype=_lib.dtype_code(query.dtype), cos_sin_dtype=_lib.dtype_code(cos_sin_cache.dtype),
         position_dtype=_lib.dtype_code(positions.dtype), slot_dtype=_lib.dtype_code(slot_mapping.dtype),
+        key_out=None, cache_dtype=_lib.dtype_code(query.dtype),
     )
     with torch.cuda.device(query.device):
         _lib.check(lib.b200_rope_kv_write(ctypes.byref(p), _lib.current_stream(query.device)), "fused_rope_and_cache")

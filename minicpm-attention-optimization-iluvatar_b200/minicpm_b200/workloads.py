@@ -287,3 +287,120 @@ def rope_algorithmic_bytes(b: RopeBatch) -> int:
     cs = t * b.rotary_dim * b.cos_sin_cache.element_size()
     idx = t * (b.positions.element_size() + b.slot_mapping.element_size())
     return q_bytes + kv_read + kv_write + cs + idx
+
+
+# ---------------------------------------------------------------------------
+# Paged KV-cache write (the service's cache update).
+# ---------------------------------------------------------------------------
+
+# kv_cache_dtype string -> (cache torch dtype, inline scale padding in elements)
+KV_CACHE_KINDS = {
+    "auto": (None, 0),
+    "fp8": (torch.float8_e4m3fn, 0),
+    "int8_per_token_head": (torch.int8, 4),
+    "fp8_per_token_head": (torch.float8_e4m3fn, 4),
+}
+
+
+@dataclass
+class KvWriteBatch:
+    key: torch.Tensor  # [T, KH, D]
+    value: torch.Tensor  # [T, KH, D]
+    slot_mapping: torch.Tensor  # [T]; negative = padding token
+    kv_cache: torch.Tensor  # [num_blocks, 2, block_size, KH, D + pad], sentinel-filled
+    kv_cache_dtype: str
+    k_scale: torch.Tensor  # [1] float32 (fp8 per-tensor)
+    v_scale: torch.Tensor
+
+    def to(self, device) -> "KvWriteBatch":
+        return KvWriteBatch(**{k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in self.__dict__.items()})
+
+    def clone(self) -> "KvWriteBatch":
+        return KvWriteBatch(**{k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in self.__dict__.items()})
+
+    @property
+    def head_dim(self) -> int:
+        return self.key.shape[2]
+
+    def caches(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """``kv_cache.unbind(1)`` trimmed to head_dim: the data part of each cache row."""
+        k, v = self.kv_cache.unbind(1)
+        d = self.head_dim
+        return k[..., :d], v[..., :d]
+
+    def scale_cache_views(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """float32 views ``[num_blocks, block_size, KH]`` of the inline per-token-head scales.
+
+        The scale of (block, slot, head) is the float32 in the 4 bytes after
+        head_dim of that cache row, as the service's ``_ensure_scale_caches``
+        lays it out (integration/vllm-plugin-FL-split-kv.patch:473-523).
+        """
+        nb, _, bs, kh, padded = self.kv_cache.shape
+        e = self.kv_cache.element_size()
+        row = padded * e
+        assert row % 4 == 0 and (self.kv_cache.storage_offset() * e) % 4 == 0
+        base = torch.empty(0, dtype=torch.float32, device=self.kv_cache.device).set_(self.kv_cache.untyped_storage())
+        half = bs * kh * row
+        start = self.kv_cache.storage_offset() * e // 4 + self.head_dim * e // 4
+        stride = (2 * half // 4, kh * row // 4, row // 4)
+        ks = torch.as_strided(base, (nb, bs, kh), stride, start)
+        vs = torch.as_strided(base, (nb, bs, kh), stride, start + half // 4)
+        return ks, vs
+
+
+def build_kv_write_batch(
+    tokens: int = 16384,
+    *,
+    kv_cache_dtype: str = "auto",
+    num_kv_heads: int = NUM_KV_HEADS,
+    head_dim: int = HEAD_DIM,
+    block_size: int = BLOCK_SIZE,
+    num_blocks: int = 4096,
+    padding_tokens: int = 0,
+    seed: int = DEFAULT_SEED,
+    dtype: torch.dtype = torch.bfloat16,
+    slot_dtype: torch.dtype = torch.int64,
+    k_scale: float = 0.0125,
+    v_scale: float = 0.0089,
+) -> KvWriteBatch:
+    """New K/V rows scattered by a seeded injection into a sentinel-filled 5-D cache.
+
+    Values are N(0, 1) with every 16th (token, head) row scaled by 20 so the
+    per-token-head scales vary and the per-tensor fp8 path meets saturation.
+    The last ``padding_tokens`` tokens get slot -1.
+    """
+    g = _gen(seed, 47, tokens, num_kv_heads, head_dim, len(kv_cache_dtype))
+    boost = torch.ones(tokens, num_kv_heads, 1)
+    boost.view(-1)[::16] = 20.0
+    key = (torch.randn(tokens, num_kv_heads, head_dim, generator=g) * boost).to(dtype)
+    value = (torch.randn(tokens, num_kv_heads, head_dim, generator=g) * boost.flip(0)).to(dtype)
+    slots = torch.randperm(num_blocks * block_size, generator=g)[:tokens]
+    if padding_tokens:
+        slots[tokens - padding_tokens :] = -1
+    cache_dtype, pad = KV_CACHE_KINDS[kv_cache_dtype]
+    cache_dtype = cache_dtype or dtype
+    shape = (num_blocks, 2, block_size, num_kv_heads, head_dim + pad)
+    if cache_dtype in (torch.int8, torch.float8_e4m3fn):
+        kv_cache = torch.full(shape, 0x5A, dtype=torch.uint8).view(cache_dtype)
+    else:
+        kv_cache = torch.full(shape, 7.0, dtype=cache_dtype)
+    return KvWriteBatch(
+        key=key,
+        value=value,
+        slot_mapping=slots.to(slot_dtype),
+        kv_cache=kv_cache,
+        kv_cache_dtype=kv_cache_dtype,
+        k_scale=torch.tensor([k_scale], dtype=torch.float32),
+        v_scale=torch.tensor([v_scale], dtype=torch.float32),
+    )
+
+
+def kv_write_algorithmic_bytes(b: KvWriteBatch) -> int:
+    """K and V read, K and V cache rows (plus per-token-head scales) written, slots read."""
+    t, kh, d = b.key.shape
+    written = int((b.slot_mapping >= 0).sum())
+    read = 2 * t * kh * d * b.key.element_size()
+    write = 2 * written * kh * d * b.kv_cache.element_size()
+    if b.kv_cache_dtype.endswith("per_token_head"):
+        write += 2 * written * kh * 4
+    return read + write + t * b.slot_mapping.element_size()

@@ -8,7 +8,9 @@ Every function restates the algorithm of the reference implementation in
 plain fp32 torch/numpy on the CPU and cites the reference file and lines it
 follows.  The restatement is pinned against golden vectors produced by the
 reference's own Triton kernels run under ``TRITON_INTERPRET=1`` on the CPU
-(``tests/golden/make_golden.py``; fixtures in ``tests/golden/*.npz``).
+(``tests/golden/make_golden.py``; fixtures in ``tests/golden/*.npz``), and,
+for the service's KV-cache writes, by vLLM's Triton kernels run the same way
+(``tests/golden/make_kv_golden.py``).
 """
 
 from .paged_sdpa import (
@@ -16,6 +18,14 @@ from .paged_sdpa import (
     paged_attention_reference,
     split_kv_partials_reference,
     split_kv_reduce_reference,
+)
+from .kv_cache import (
+    fp8_decode,
+    fp8_encode,
+    kv_write_reference,
+    quantize_per_tensor,
+    quantize_per_token_head,
+    rope_and_cache_service_reference,
 )
 from .rope import reference_rope, rope_and_cache_reference, rotate_fp32
 
@@ -27,4 +37,10 @@ __all__ = [
     "reference_rope",
     "rope_and_cache_reference",
     "rotate_fp32",
+    "fp8_encode",
+    "fp8_decode",
+    "quantize_per_tensor",
+    "quantize_per_token_head",
+    "kv_write_reference",
+    "rope_and_cache_service_reference",
 ]

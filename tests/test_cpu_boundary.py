@@ -41,7 +41,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for name in declared:
         assert hasattr(lib, name), f"{name} declared in include/ but not exported"
     assert set(_lib.EXPORTED_SYMBOLS) <= declared
-    assert lib.b200_abi_version() == 1
+    assert lib.b200_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_host_only_entry_points():

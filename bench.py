@@ -48,12 +48,18 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="chunked_prefill_16k",
-                    choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "rope_16384"])
+                    choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "rope_16384",
+                             "kv_write_16384"])
     ap.add_argument("--splits", type=int, default=0, help="0 = automatic")
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="keep only the first N sequences of the workload (small cases for profiling)")
     ap.add_argument("--rotary-dim", type=int, default=128)
     ap.add_argument("--interleaved", action="store_true")
+    ap.add_argument("--kv-dtype", default="auto",
+                    choices=["auto", "fp8", "int8_per_token_head", "fp8_per_token_head"],
+                    help="kv_write_16384: the cache kind; rope_16384 --service: auto or fp8")
+    ap.add_argument("--service", action="store_true",
+                    help="rope_16384: the service's rope-and-cache call (key rotated in place)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--verify", action="store_true", help="gather outputs to rank 0 (NCCL) and check sampled rows")
@@ -269,41 +275,198 @@ def reference_arm(args, world, rank):
 
 # --------------------------------------------------------------------- RoPE bench
 def rope_bench(args, world, rank, local):
-    from minicpm_b200 import fused_rope_and_cache
+    """RoPE + paged KV-cache write of 16384 tokens (the reference operator, or with
+    ``--service`` the service's call: key rotated in place, ``--kv-dtype fp8`` caches)."""
+    from minicpm_b200 import fused_rope_and_cache, kv_cache
     from minicpm_b200.workloads import build_rope_batch, rope_algorithmic_bytes
 
+    dev = torch.device("cuda", local)
     b = build_rope_batch(16384, rotary_dim=args.rotary_dim, is_neox=not args.interleaved)
-    g = b.to(torch.device("cuda", local))
+    g = b.to(dev)
     nbytes = rope_algorithmic_bytes(b)
+    fp8 = args.service and args.kv_dtype == "fp8"
+    if args.service:
+        t, hkv, d = b.key.shape
+        written = int((b.slot_mapping >= 0).sum())
+        nbytes += 2 * t * hkv * args.rotary_dim * b.key.element_size()  # rotated key written back
+        if fp8:
+            nbytes -= 2 * written * hkv * d * (b.key.element_size() - 1)  # 1-byte cache rows
+            g.key_cache = torch.zeros(g.key_cache.shape, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+            g.value_cache = torch.zeros_like(g.key_cache)
+        ks = torch.tensor([0.02], device=dev)
+        vs = torch.tensor([0.015], device=dev)
+
     def step():
-        fused_rope_and_cache(g.query, g.key, g.value, g.positions, g.cos_sin_cache, g.is_neox, g.key_cache,
-                             g.value_cache, g.slot_mapping)
+        if args.service:
+            kv_cache.rope_and_cache(g.query, g.key, g.value, g.positions, g.cos_sin_cache, g.is_neox, g.key_cache,
+                                    g.value_cache, g.slot_mapping, ks, vs, True, fp8)
+        else:
+            fused_rope_and_cache(g.query, g.key, g.value, g.positions, g.cos_sin_cache, g.is_neox, g.key_cache,
+                                 g.value_cache, g.slot_mapping)
 
     for _ in range(args.warmup):
         step()
-    barrier(world)
-    # Back-to-back launches: the 172 MB the kernel moves exceed the 126 MB L2,
-    # so each launch streams from HBM (and writes back what the previous left).
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(args.steps):
-        step()
-    e.record()
-    e.synchronize()
-    ms = max_over_ranks(s.elapsed_time(e) / args.steps, world)
+    # Back-to-back launches replayed from a CUDA graph: the ~170 MB one launch
+    # moves exceed the 126 MB L2, so each launch streams from HBM.
+    ms, clocks = graph_timed(lambda i: step(), args.steps, local, world)
     peaks, kind = measured_peaks()
     gbs = nbytes / (ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = rope_cpu_baseline(b, nbytes)
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": "RoPE + paged KV-cache write GB/s", "value": gbs * world, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "rope_16384", "tokens": 16384, "rotary_dim": args.rotary_dim,
-                       "is_neox": not args.interleaved, "algorithmic_bytes": nbytes, "l2": "inputs larger than L2, back-to-back launches"},
+                       "is_neox": not args.interleaved, "service": bool(args.service),
+                       "cache": "fp8_e4m3" if fp8 else "bf16", "algorithmic_bytes": nbytes,
+                       "l2": "inputs larger than L2, back-to-back launches",
+                       "timing": "CUDA graph of all timed launches, replayed once"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": kind},
+            "clocks": clocks,
             "gpu_launches": args.steps,
-        }), flush=True)
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def rope_cpu_baseline(b, nbytes):
+    """The oracle's RoPE + cache write on the first 2048 of the 16384 tokens, on the host cores."""
+    from oracle import rope_and_cache_reference
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    n = 2048
+
+    def run():
+        rope_and_cache_reference(b.query[:n], b.key[:n], b.value[:n], b.positions[:n], b.cos_sin_cache, b.is_neox,
+                                 b.key_cache, b.value_cache, b.slot_mapping[:n], b.rotary_dim)
+
+    run()
+    times = time_cpu(run, 3)
+    sec = sum(times) / len(times)
+    return {"value": nbytes * n / b.query.shape[0] / sec / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"first {n} of 16384 tokens, 3 repetitions (bytes scaled to the sample)"}
+
+
+# --------------------------------------------------------------------- graph-timed short kernels
+def graph_timed(step, steps: int, local: int, world: int):
+    """Device time per launch of ``step(i)``, i = 0..steps-1, captured in one CUDA graph.
+
+    Kernels of a few to tens of microseconds launched one by one from Python
+    would be timed behind the host's launch overhead; replaying the captured
+    sequence keeps the GPU busy back to back.  Returns (ms per launch, clocks).
+    """
+    stream = torch.cuda.Stream(device=local)
+    stream.wait_stream(torch.cuda.current_stream(local))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                step(i)
+    torch.cuda.current_stream(local).wait_stream(stream)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(local)
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        s.record()
+        graph.replay()
+        e.record()
+        e.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / steps, world)
+    del graph
+    return ms, clocks.summary()
+
+
+# --------------------------------------------------------------------- KV-cache write bench
+KV_ROTATION = 8  # distinct input sets cycled by the timed loop
+
+
+def kv_write_bench(args, world, rank, local):
+    """The service's cache update on 16384 new tokens (16 KV-head-dim rows of 2 heads each).
+
+    One launch of 16384 tokens moves ~33 MB, less than the 126 MB L2, so the
+    timed loop cycles through 8 independent batches (distinct K/V rows and slot
+    sets; ~190 MB of distinct bytes with the 64 MB cache) back to back.
+    """
+    from minicpm_b200 import kv_cache
+    from minicpm_b200.workloads import build_kv_write_batch, kv_write_algorithmic_bytes
+
+    dev = torch.device("cuda", local)
+    kind = args.kv_dtype
+    first = build_kv_write_batch(16384, kv_cache_dtype=kind)
+    shared_cache = first.kv_cache.to(dev)
+    batches = []
+    for r in range(KV_ROTATION):
+        b = build_kv_write_batch(16384, kv_cache_dtype=kind, seed=1000 + r, num_blocks=4096)
+        g = b.to(dev)
+        g.kv_cache = shared_cache
+        batches.append(g)
+    nbytes = kv_write_algorithmic_bytes(first)
+
+    def step(i):
+        g = batches[i % KV_ROTATION]
+        kc, vc = g.caches()
+        if kind.endswith("per_token_head"):
+            ks, vs = g.scale_cache_views()
+            kv_cache.reshape_and_cache_flash_per_token_head_quant(g.key, g.value, kc, vc, ks, vs, g.slot_mapping)
+        else:
+            kv_cache.reshape_and_cache_flash(g.key, g.value, kc, vc, g.slot_mapping, kind, g.k_scale, g.v_scale)
+
+    for i in range(max(args.warmup, KV_ROTATION)):
+        step(i)
+    # One step = one pass over the rotating input sets (KV_ROTATION launches).
+    ms, clocks = graph_timed(step, args.steps * KV_ROTATION, local, world)
+    peaks, pkind = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = kv_write_cpu_baseline(first, nbytes)
+    if rank == 0:
+        line = {
+            "metric": "paged KV-cache write GB/s", "value": gbs * world, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms * KV_ROTATION, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": str(first.key.dtype).replace("torch.", ""),
+            "data": "synthetic",
+            "config": {"workload": "kv_write_16384", "tokens": 16384, "kv_heads": 2, "head_dim": 128,
+                       "kv_cache_dtype": kind, "algorithmic_bytes_per_launch": nbytes,
+                       "launches_per_step": KV_ROTATION, "us_per_launch": ms * 1e3,
+                       "timing": "CUDA graph of all timed launches, replayed once",
+                       "l2": f"{KV_ROTATION} rotating input sets, footprint larger than L2, back-to-back launches"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": pkind},
+            "clocks": clocks,
+            "gpu_launches": args.steps * KV_ROTATION,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def kv_write_cpu_baseline(b, nbytes):
+    """The oracle's cache write of the same 16384 tokens, timed on the host cores."""
+    from oracle import kv_write_reference
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    kc, vc = b.caches()
+    ksc = vsc = None
+    if b.kv_cache_dtype.endswith("per_token_head"):
+        ksc, vsc = (t.clone() for t in b.scale_cache_views())
+
+    def run():
+        kv_write_reference(b.key, b.value, kc, vc, b.slot_mapping, b.kv_cache_dtype, float(b.k_scale),
+                           float(b.v_scale), ksc, vsc)
+
+    run()
+    times = time_cpu(run, 3)
+    sec = sum(times) / len(times)
+    return {"value": nbytes / sec / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": "the full 16384-token write, 3 repetitions"}
 
 
 # --------------------------------------------------------------------- verification
@@ -499,6 +662,8 @@ def main():
     try:
         if args.workload == "rope_16384":
             rope_bench(args, world, rank, local)
+        elif args.workload == "kv_write_16384":
+            kv_write_bench(args, world, rank, local)
         else:
             attention_bench(args, world, rank, local)
     finally:

@@ -550,6 +550,18 @@ int b200_kv_cache_write(const B200KvWriteParams* p, void* stream) {
   a.num_slots = (int64_t)p->num_blocks * p->block_size;
   a.num_tokens = p->num_tokens; a.hkv = p->num_kv_heads; a.head_dim = p->head_dim; a.block_size = p->block_size;
   a.slot_i64 = p->slot_dtype == B200_DTYPE_I64;
+  const int64_t n_items = (int64_t)p->num_tokens * p->num_kv_heads * (p->head_dim / 8);
+  if (n_items >= (int64_t(1) << 31) || a.num_slots >= (int64_t(1) << 31))
+    return fail(B200_ERR_UNSUPPORTED, "more than 2^31 chunks or cache slots in one KV-cache write");
+  auto log2_or = [](int64_t v) {
+    if (v <= 0 || (v & (v - 1))) return -1;
+    int k = 0;
+    while ((int64_t(1) << k) < v) ++k;
+    return k;
+  };
+  a.total_items = (uint32_t)n_items;
+  a.n_shift = log2_or((int64_t)p->num_kv_heads * (p->head_dim / 8));
+  a.bs_shift = log2_or(p->block_size);
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto launch = [&](auto kernel) {
@@ -557,24 +569,30 @@ int b200_kv_cache_write(const B200KvWriteParams* p, void* stream) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, b200::kKvWriteThreads, 0) != cudaSuccess ||
         per_sm <= 0)
       per_sm = 1;
-    const int64_t warps_per_cta = b200::kKvWriteThreads / 32;
     const int64_t resident = (int64_t)sm_count() * per_sm;
-    const int64_t needed = (p->num_tokens + warps_per_cta - 1) / warps_per_cta;
+    const int64_t needed = (n_items + b200::kKvWriteThreads - 1) / b200::kKvWriteThreads;
     kernel<<<dim3((unsigned)std::max<int64_t>(1, std::min(resident, needed))), b200::kKvWriteThreads, 0, s>>>(a);
   };
-#define B200_KV_MODES(T)                                                                                  \
-  if (p->quant_mode == B200_KVQ_NONE) launch(b200::kv_cache_write_kernel<T, b200::kKvCopy, b200::kElemSame>); \
-  else if (p->quant_mode == B200_KVQ_FP8_PER_TENSOR) {                                                    \
-    if (elem == b200::kElemE4M3) launch(b200::kv_cache_write_kernel<T, b200::kKvFp8Tensor, b200::kElemE4M3>); \
-    else launch(b200::kv_cache_write_kernel<T, b200::kKvFp8Tensor, b200::kElemE5M2>);                       \
-  } else if (elem == b200::kElemI8) launch(b200::kv_cache_write_kernel<T, b200::kKvPerTokenHead, b200::kElemI8>); \
-  else launch(b200::kv_cache_write_kernel<T, b200::kKvPerTokenHead, b200::kElemE4M3>);
+#define B200_KV_CPR(T, MODE, ELEM)                                              \
+  switch (p->head_dim) {                                                        \
+    case 64: launch(b200::kv_cache_write_kernel<T, MODE, ELEM, 8>); break;      \
+    case 128: launch(b200::kv_cache_write_kernel<T, MODE, ELEM, 16>); break;    \
+    default: launch(b200::kv_cache_write_kernel<T, MODE, ELEM, 32>); break;     \
+  }
+#define B200_KV_MODES(T)                                                                      \
+  if (p->quant_mode == B200_KVQ_NONE) { B200_KV_CPR(T, b200::kKvCopy, b200::kElemSame) }      \
+  else if (p->quant_mode == B200_KVQ_FP8_PER_TENSOR) {                                        \
+    if (elem == b200::kElemE4M3) { B200_KV_CPR(T, b200::kKvFp8Tensor, b200::kElemE4M3) }      \
+    else { B200_KV_CPR(T, b200::kKvFp8Tensor, b200::kElemE5M2) }                              \
+  } else if (elem == b200::kElemI8) { B200_KV_CPR(T, b200::kKvPerTokenHead, b200::kElemI8) }  \
+  else { B200_KV_CPR(T, b200::kKvPerTokenHead, b200::kElemE4M3) }
   switch (p->dtype) {
     case B200_DTYPE_BF16: B200_KV_MODES(__nv_bfloat16) break;
     case B200_DTYPE_F16: B200_KV_MODES(__half) break;
     default: B200_KV_MODES(float) break;
   }
 #undef B200_KV_MODES
+#undef B200_KV_CPR
   return check_launch("kv_cache_write_kernel");
 }
 

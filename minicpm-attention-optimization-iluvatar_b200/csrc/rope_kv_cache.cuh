@@ -281,7 +281,8 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
 // Eight rotated values (fp32) to a cache row: the model dtype, or fp8 of the
 // value rounded to the model dtype and divided by the cache's scale.
 template <typename T>
-__device__ __forceinline__ void cache_store8(void* base, int64_t off, const float (&y)[8], int elem, float scale) {
+__device__ __forceinline__ void cache_store8(void* base, int64_t off, const float (&y)[8], int elem,
+                                             const FixedDivisor& scale) {
   if (elem == kElemSame) {
     store8<T>(static_cast<T*>(base) + off, y);
     return;
@@ -296,7 +297,8 @@ __device__ __forceinline__ void cache_store8(void* base, int64_t off, const floa
 
 // Eight unrotated elements (raw) to a cache row.
 template <typename T>
-__device__ __forceinline__ void cache_copy8(void* base, int64_t off, const uint4& x, int elem, float scale) {
+__device__ __forceinline__ void cache_copy8(void* base, int64_t off, const uint4& x, int elem,
+                                            const FixedDivisor& scale) {
   if (elem == kElemSame) {
     *reinterpret_cast<uint4*>(static_cast<T*>(base) + off) = x;
     return;
@@ -421,10 +423,10 @@ __global__ void __launch_bounds__(kRopeThreads, 2) rope_kv_warp_kernel(const Rop
         const int64_t blk = slot / a.block_size;
         ctok = blk * a.c_sb + (slot - blk * a.block_size) * a.c_st;
       }
-      float ks = 1.0f, vs = 1.0f;
+      FixedDivisor ks{}, vs{};
       if (a.cache_elem != kElemSame) {
-        ks = *a.k_scale;
-        vs = *a.v_scale;
+        ks = make_divisor(*a.k_scale);
+        vs = make_divisor(*a.v_scale);
       }
       T* kotok = a.ko ? static_cast<T*>(a.ko) + token * a.ko_st : nullptr;
       auto rotate_key = [&](const uint4& x1, const uint4& x2, int h) {

@@ -93,6 +93,23 @@ def test_fp8_per_tensor_cache_write(storage, dtype):
     assert ((codes & 0x7F) == 0x7E).any() and not ((codes & 0x7F) == 0x7F).any()
 
 
+@pytest.mark.parametrize("kind", ["fp8", "fp8_per_token_head", "int8_per_token_head"])
+def test_quantised_special_values(kind):
+    """Signed zeros, bf16 subnormals, tiny, huge and infinite inputs."""
+    b = build_kv_write_batch(512, kv_cache_dtype=kind, num_blocks=64)
+    specials = torch.tensor([0.0, -0.0, 1e-40, -1e-40, 3e-39, 1e-30, -1e-20, 1e30, -3e38, float("inf"),
+                             -float("inf"), 0.0125 * 448.5, -0.0125 * 464.0, 0.0125 * 0.5 ** 10],
+                            dtype=torch.float32).to(torch.bfloat16)
+    k = b.key.view(-1)
+    k[: 37 * specials.numel()] = specials.repeat(37)
+    if kind.endswith("per_token_head"):  # one head of all zeros and one of a single signed zero
+        b.key[100, 0].zero_()
+        b.key[101, 1].zero_()
+        b.key[101, 1, 5] = -0.0
+        b.key[:20] = torch.where(torch.isinf(b.key[:20].float()), torch.zeros(()), b.key[:20].float()).to(b.key.dtype)
+    _check_write(b, _run_write(b))
+
+
 def test_fp8_e5m2_through_the_c_abi():
     b = build_kv_write_batch(1024, kv_cache_dtype="fp8", num_blocks=128, padding_tokens=4)
     b.kv_cache = b.kv_cache.view(torch.float8_e5m2)

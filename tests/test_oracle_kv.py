@@ -126,3 +126,47 @@ def test_kv_cache_validation_on_cpu():
     with pytest.raises(NotImplementedError):
         kv_cache.rope_and_cache(b.key, b.key, b.value, b.slot_mapping, b.k_scale, True, kc, vc, b.slot_mapping,
                                 b.k_scale, b.v_scale, False, False)
+
+
+def _rn32(f):
+    """Round an exact rational to the nearest binary32 (ties to even); normal range only."""
+    from fractions import Fraction
+
+    if f == 0:
+        return 0.0
+    sign = -1 if f < 0 else 1
+    a = abs(Fraction(f))
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    if a < Fraction(2) ** e:
+        e -= 1
+    m = a / Fraction(2) ** (e - 23)  # in [2^23, 2^24)
+    n = m.numerator // m.denominator
+    rem = m - n
+    if rem > Fraction(1, 2) or (rem == Fraction(1, 2) and n % 2):
+        n += 1
+    return sign * float(Fraction(n) * Fraction(2) ** (e - 23))
+
+
+def test_fixed_divisor_quotient_is_correctly_rounded():
+    """The kernels' x / s for a per-launch scale (the fp8 per-tensor caches): y = RN(1/s),
+    q = RN(x y), then twice q <- RN(q + RN_exact(x - s q) y) with exact FMA residuals.
+    Checked against the correctly rounded quotient with exact rational arithmetic."""
+    from fractions import Fraction
+
+    rng = np.random.default_rng(11)
+    bf16 = (np.arange(65536, dtype=np.uint32) << 16).view(np.float32)
+    bf16 = bf16[np.isfinite(bf16) & (np.abs(bf16) > 1e-30) & (np.abs(bf16) < 1e30)]
+    for s in [0.0125, 0.0089, 0.0173, 0.0121, 1 / 3, 0.37, float(rng.uniform(1e-3, 10))]:
+        s = float(np.float32(s))
+        fs = Fraction(s)
+        y = _rn32(1 / fs)
+        fy = Fraction(y)
+        xs = np.concatenate([rng.choice(bf16, 1500), (rng.standard_normal(1500) * 50).astype(np.float32)])
+        for x in xs.tolist():
+            fx = Fraction(x)
+            q = _rn32(fx * fy)
+            for _ in range(2):
+                r = _rn32(fx - fs * Fraction(q))  # exact in binary32 (an FMA residual)
+                assert Fraction(r) == fx - fs * Fraction(q)
+                q = _rn32(Fraction(q) + Fraction(r) * fy)
+            assert q == _rn32(fx / fs), (x, s)

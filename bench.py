@@ -48,8 +48,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="chunked_prefill_16k",
-                    choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "rope_16384",
-                             "kv_write_16384"])
+                    choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "decode_16k", "decode_4k",
+                             "rope_16384", "kv_write_16384"])
     ap.add_argument("--splits", type=int, default=0, help="0 = automatic")
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="keep only the first N sequences of the workload (small cases for profiling)")
@@ -509,9 +509,14 @@ def attention_bench(args, world, rank, local):
     from minicpm_b200.split_kv_paged import choose_num_splits
     from oracle import causal_flops  # FLOP formula of the reference harness (no compute)
 
+    from minicpm_b200.workloads import attention_kv_bytes
+
     dev = torch.device("cuda", local)
+    decode = args.workload.startswith("decode")
     batch, all_q, all_kv = build_local_batch(args.workload, world, rank, args.num_seqs)
     local_flops = causal_flops(batch.query_lens, batch.kv_lens, 16, 128)
+    local_bytes = attention_kv_bytes(batch.query_lens, batch.kv_lens)
+    total_bytes = sum_over_ranks(float(local_bytes), world) if world > 1 else float(local_bytes)
     total_flops = sum_over_ranks(float(local_flops), world) if world > 1 else float(local_flops)
     total_tokens = sum(all_q)
     g = batch.to(dev)
@@ -610,8 +615,13 @@ def attention_bench(args, world, rank, local):
         run, flops_s, desc = cpu_sample_flops(batch, 512)
         run()
         ts = time_cpu(run, 2)
-        cpu = {"value": flops_s / statistics.mean(ts) / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-               "kind": "port", "sample": desc}
+        if decode:
+            sample_bytes = attention_kv_bytes([1], [batch.kv_lens[0]])
+            cpu = {"value": sample_bytes / statistics.mean(ts) / 1e9, "unit": "GB/s",
+                   "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
+        else:
+            cpu = {"value": flops_s / statistics.mean(ts) / 1e12, "unit": "TFLOP/s",
+                   "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
     l2_note = "inputs larger than L2 (KV %.0f MB + Q %.0f MB per GPU)" % (
         g.kv_cache.numel() * 2 / 1e6 * (1 if world == 1 else 1), g.q.numel() * 2 / 1e6)
     line = {
@@ -648,6 +658,22 @@ def attention_bench(args, world, rank, local):
         "clocks": clocks.summary(),
         "gpu_launches": args.steps * (2 + (1 if resolved > 1 else 0)),
     }
+    if decode:
+        # Decode streams every K/V row once for a handful of query rows: the
+        # bound is HBM, and the metric is the bytes moved per second.
+        gbs = total_bytes * args.steps / (max_ms * 1e-3) / 1e9
+        achieved_gbs = local_bytes / (launch_ms * 1e-3) / 1e9
+        line.update({
+            "metric": "paged decode attention GB/s (K/V streamed once)", "value": gbs, "unit": "GB/s",
+            "tc_peak_frac": None, "decode_tokens_per_s": tokens_per_s,
+            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": peak_kind,
+                         "per_launch_ms": launch_ms, "launch": "schedule + attention (+ combine) kernels of one call"},
+        })
+        line["config"]["algorithmic_bytes"] = total_bytes
+        if e2e:
+            e2e["value"] = total_bytes * args.steps / (e2e["ms_per_step"] * args.steps * 1e-3) / 1e9
+            e2e["unit"] = "GB/s"
     print(json.dumps(line), flush=True)
 
 

@@ -83,6 +83,7 @@ extern "C" {
 #define B200_DEVERR_WAIT_TIMEOUT 1u /* an in-kernel wait ran past its limit     */
 #define B200_DEVERR_SLOT_RANGE 2u   /* slot_mapping entry >= num_blocks*bs      */
 #define B200_DEVERR_POS_RANGE 3u    /* position outside the cos/sin table        */
+#define B200_DEVERR_DECODE_QLEN 4u  /* max_seqlen_q = 1 but a sequence has more query tokens */
 
 /*
  * Paged causal varlen attention (prefill / chunked prefill), GQA, Split-KV.
@@ -94,7 +95,9 @@ extern "C" {
  * out        [total_q, num_q_heads, head_dim], written in place
  * block_table [num_seqs, block_table_cols], int32 or int64, row stride in elements
  * cu_seqlens_q [num_seqs + 1], seqused_k [num_seqs]: int32 or int64
- * num_splits  0 = choose automatically, else 1..16
+ * num_splits  0 = choose automatically, else 1..16.  A decode batch (max_seqlen_q == 1)
+ *             runs the decode kernel, which splits the keys of each sequence into
+ *             chunks of its own choosing; num_splits does not change the result.
  * workspace   device buffer of at least b200_attn_workspace_bytes(...) bytes,
  *             owned by the caller; must not be shared by calls that overlap.
  * All pointers: 16-byte aligned; all strides except d: multiples of 8 elements.

@@ -22,6 +22,7 @@
 #include "minicpm_b200.h"
 #include "paged_attention.cuh"
 #include "paged_attention_pair.cuh"
+#include "paged_decode.cuh"
 #include "rope_kv_cache.cuh"
 #include "split_combine.cuh"
 #include "kv_cache_write.cuh"
@@ -111,6 +112,44 @@ WorkspaceLayout attn_workspace_layout(int64_t total_q, int num_seqs, int hq, int
   return w;
 }
 
+// Decode batches (one query token per sequence): keys per work item, chosen so
+// that the persistent grid gets about eight items per CTA.
+int decode_chunk(int num_seqs, int hkv, int max_k, int num_sms) {
+  const int64_t work = (int64_t)num_seqs * hkv * std::max(max_k, 1);
+  const int64_t target = (int64_t)8 * std::max(num_sms, 1);
+  int64_t c = (work + target - 1) / target;
+  c = (c + b200::kDecTileN - 1) / b200::kDecTileN * b200::kDecTileN;
+  return (int)std::min<int64_t>(std::max<int64_t>(c, 2 * b200::kDecTileN), int64_t(1) << 24);
+}
+
+struct DecodeLayout {
+  size_t base_off, m_off, l_off, o_off, total;
+  int chunk;
+  int64_t items_ub;
+};
+
+DecodeLayout decode_layout(int num_seqs, int hkv, int group, int max_k, int num_sms) {
+  DecodeLayout d{};
+  d.chunk = decode_chunk(num_seqs, hkv, max_k, num_sms);
+  d.items_ub = (int64_t)num_seqs * hkv * ((std::max(max_k, 0) + d.chunk - 1) / d.chunk);
+  d.base_off = 0;
+  d.m_off = align_up(sizeof(int) * (size_t)(num_seqs + 1), 256);
+  d.l_off = align_up(d.m_off + sizeof(float) * (size_t)d.items_ub * group, 256);
+  d.o_off = align_up(d.l_off + sizeof(float) * (size_t)d.items_ub * group, 256);
+  d.total = align_up(d.o_off + sizeof(float) * (size_t)d.items_ub * group * b200::kAttnHeadDim, 256);
+  return d;
+}
+
+bool decode_shape_ok(int group, int hkv) {
+  return (group == 4 || group == 8 || group == 16) && hkv <= b200::kDecMaxKvHeads;
+}
+
+// B200_ATTN_DECODE=0 sends decode batches through the prefill kernel instead.
+bool use_decode_kernel() {
+  const char* e = getenv("B200_ATTN_DECODE");
+  return !(e && e[0] == '0');
+}
+
 // B200_ATTN_CTA_PAIR=1 selects the CTA-pair attention kernel, 0 the single-CTA one.
 bool use_cta_pair() {
   const char* e = getenv("B200_ATTN_CTA_PAIR");
@@ -131,6 +170,90 @@ int auto_splits(int32_t total_q, int32_t num_seqs, int32_t hq, int32_t hkv, int3
   return s;
 }
 
+// Decode batch: schedule (items per sequence), persistent decode kernel, combine.
+int run_decode(const B200AttnParams* p, cudaStream_t s, int group) {
+  const int elt = 2;
+  const int sms = sm_count();
+  const DecodeLayout dl = decode_layout(p->num_seqs, p->num_kv_heads, group, p->max_seqlen_k, sms);
+  if (!p->workspace || p->workspace_bytes < dl.total)
+    return fail(B200_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", dl.total, p->workspace_bytes);
+  if (dl.items_ub == 0) return B200_OK;
+  uint8_t* ws = static_cast<uint8_t*>(p->workspace);
+  const CUtensorMapDataType dt =
+      p->dtype == B200_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tm_q;
+  {
+    const cuuint64_t dims[3] = {(cuuint64_t)p->head_dim, (cuuint64_t)p->num_q_heads, (cuuint64_t)p->total_q};
+    const cuuint64_t strides[2] = {(cuuint64_t)(p->q_stride_h * elt), (cuuint64_t)(p->q_stride_t * elt)};
+    const cuuint32_t box[3] = {64, (cuuint32_t)group, 1};
+    if (int r = encode_map(&tm_q, dt, 3, p->q, dims, strides, box, "q")) return r;
+  }
+  // Per KV head: (d, key % 8, half of head_dim, key / 8 in the page, page); one
+  // box = a 16-key page slice with both halves (4 KB).
+  b200::DecodeMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  for (int h = 0; h < p->num_kv_heads; ++h) {
+    for (int kv = 0; kv < 2; ++kv) {
+      const uint8_t* base = static_cast<const uint8_t*>(kv ? p->v : p->k) +
+                            (int64_t)h * (kv ? p->v_stride_head : p->k_stride_head) * elt;
+      const int64_t st = kv ? p->v_stride_tok : p->k_stride_tok, sb = kv ? p->v_stride_block : p->k_stride_block;
+      const cuuint64_t dims[5] = {64, 8, 2, (cuuint64_t)(p->block_size / 8), (cuuint64_t)p->num_blocks};
+      const cuuint64_t strides[4] = {(cuuint64_t)(st * elt), 128, (cuuint64_t)(8 * st * elt), (cuuint64_t)(sb * elt)};
+      const cuuint32_t box[5] = {64, 8, 2, 2, 1};
+      if (int r = encode_map(kv ? &maps.v[h] : &maps.k[h], dt, 5, base, dims, strides, box, kv ? "v" : "k")) return r;
+    }
+  }
+  b200::DecodeArgs a{};
+  a.block_table = p->block_table;
+  a.cu_q = p->cu_seqlens_q;
+  a.seqused = p->seqused_k;
+  a.item_base = reinterpret_cast<int*>(ws + dl.base_off);
+  a.part_m = reinterpret_cast<float*>(ws + dl.m_off);
+  a.part_l = reinterpret_cast<float*>(ws + dl.l_off);
+  a.part_o = reinterpret_cast<float*>(ws + dl.o_off);
+  a.bt_stride = p->block_table_stride;
+  a.bt_cols = p->block_table_cols;
+  a.bt_i64 = p->block_table_dtype == B200_DTYPE_I64;
+  a.len_i64 = p->seqlen_dtype == B200_DTYPE_I64;
+  a.num_seqs = p->num_seqs;
+  a.num_kv_heads = p->num_kv_heads;
+  a.chunk = dl.chunk;
+  a.block_size = p->block_size;
+  a.num_blocks = p->num_blocks;
+  a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
+
+  b200::decode_schedule_kernel<<<1, b200::kSchedThreads, 0, s>>>(a);
+  if (int r = check_launch("decode_schedule_kernel")) return r;
+  const dim3 grid((unsigned)std::min<int64_t>(sms, dl.items_ub));
+  auto launch = [&](auto kernel) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kDecodeSmemAlloc);
+    kernel<<<grid, b200::kDecThreads, b200::kDecodeSmemAlloc, s>>>(tm_q, maps, a);
+  };
+  auto launch_combine = [&](auto kernel) {
+    const int64_t warps = (int64_t)p->num_seqs * p->num_q_heads;
+    kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a, p->out, p->out_stride_t, p->out_stride_h, p->num_q_heads);
+  };
+#define B200_DECODE_G(T)                                                                          \
+  switch (group) {                                                                                \
+    case 4: launch(b200::paged_decode_kernel<T, 4>); break;                                       \
+    case 8: launch(b200::paged_decode_kernel<T, 8>); break;                                       \
+    default: launch(b200::paged_decode_kernel<T, 16>); break;                                     \
+  }                                                                                               \
+  if (int r = check_launch("paged_decode_kernel")) return r;                                      \
+  switch (group) {                                                                                \
+    case 4: launch_combine(b200::decode_combine_kernel<T, 4>); break;                             \
+    case 8: launch_combine(b200::decode_combine_kernel<T, 8>); break;                             \
+    default: launch_combine(b200::decode_combine_kernel<T, 16>); break;                           \
+  }
+  if (p->dtype == B200_DTYPE_BF16) {
+    B200_DECODE_G(__nv_bfloat16)
+  } else {
+    B200_DECODE_G(__half)
+  }
+#undef B200_DECODE_G
+  return check_launch("decode_combine_kernel");
+}
+
 }  // namespace
 
 extern "C" {
@@ -148,7 +271,13 @@ size_t b200_attn_workspace_bytes(int32_t total_q, int32_t num_seqs, int32_t num_
                                  int32_t head_dim, int32_t num_splits, int32_t max_seqlen_k, int32_t dtype) {
   if (num_splits <= 0) num_splits = b200_choose_num_splits(total_q, num_seqs, num_q_heads, num_kv_heads, max_seqlen_k);
   const int elt = (dtype == B200_DTYPE_F32) ? 4 : 2;
-  return attn_workspace_layout(total_q, num_seqs, num_q_heads, num_kv_heads, head_dim, num_splits, elt).total;
+  size_t bytes = attn_workspace_layout(total_q, num_seqs, num_q_heads, num_kv_heads, head_dim, num_splits, elt).total;
+  // A batch with at most one query token per sequence may run the decode kernel.
+  if (total_q <= num_seqs && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0 &&
+      decode_shape_ok(num_q_heads / num_kv_heads, num_kv_heads))
+    bytes = std::max(bytes, decode_layout(num_seqs, num_kv_heads, num_q_heads / num_kv_heads, max_seqlen_k,
+                                          sm_count()).total);
+  return bytes;
 }
 
 int b200_split_combine(const B200CombineParams* p, void* stream) {
@@ -262,6 +391,8 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   }
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->max_seqlen_q == 1 && decode_shape_ok(group, p->num_kv_heads) && use_decode_kernel())
+    return run_decode(p, s, group);
   // CTA-pair kernel (M = 256 UMMA across two SMs) or single-CTA kernel.
   const bool pair = use_cta_pair();
   const int units_per_tile_group = pair ? b200::kPairTilesPerUnit : b200::kAttnTilesPerUnit;

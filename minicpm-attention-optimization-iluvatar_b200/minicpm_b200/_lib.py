@@ -43,6 +43,7 @@ DEVERR_NONE = 0
 DEVERR_WAIT_TIMEOUT = 1
 DEVERR_SLOT_RANGE = 2
 DEVERR_POS_RANGE = 3
+DEVERR_DECODE_QLEN = 4
 
 _TORCH_DTYPES = {
     torch.float16: DTYPE_F16,

@@ -15,10 +15,15 @@ same signature, same feature guards, same routing, same exceptions.
   (``kernels/attention.py:112-117``).  That route is vLLM's own kernel and is
   not part of this package.
 
-Difference: the two enable flags are read at every call rather than once at
+Differences: the two enable flags are read at every call rather than once at
 import (the reference's service twin reads them per call too), so a process
 can switch paths without re-importing.  ``ILUVATAR_NUM_SPLITS`` unset means
-an automatically chosen split count instead of 4.
+an automatically chosen split count instead of 4.  ``ILUVATAR_SPLIT_KV_DECODE=1``
+(new, off by default, so the reference's routing is kept unless asked for)
+sends pure-decode calls (``max_seqlen_q == 1``) to the sm_100a decode kernel
+instead of vLLM; the reference left decode on vLLM and its own decode
+experiment (``experiments/patches/2026-10-09-native-decode-unvalidated.patch``)
+was never validated.
 """
 
 from __future__ import annotations
@@ -41,6 +46,10 @@ def use_optimized() -> bool:
 
 def split_kv_enabled() -> bool:
     return _flag("ILUVATAR_SPLIT_KV")
+
+
+def decode_enabled() -> bool:
+    return _flag("ILUVATAR_SPLIT_KV_DECODE")
 
 
 def _vllm_unified_attention():
@@ -104,7 +113,8 @@ def iluvatar_attention(
     use_baseline = (
         not use_optimized()
         or not split_kv_enabled()
-        or max_seqlen_q <= 1
+        or max_seqlen_q < 1
+        or (max_seqlen_q == 1 and not decode_enabled())
         or softcap != 0.0
         or kv_quant_mode != 0
         or alibi_slopes is not None

@@ -183,12 +183,36 @@ def lengths_mixed(seed: int = DEFAULT_SEED, num_seqs: int = 256) -> tuple[list[i
     return qlen.tolist(), kv.tolist()
 
 
+def lengths_decode_16k(seed: int = DEFAULT_SEED, num_seqs: int = 64) -> tuple[list[int], list[int]]:
+    """64 decode rows (one new token each), total KV length uniform in [8192, 16384]."""
+    g = _gen(seed, 16384, 1)
+    kv = torch.randint(8192, 16384 + 1, (num_seqs,), generator=g).tolist()
+    return [1] * num_seqs, kv
+
+
+def lengths_decode_4k(seed: int = DEFAULT_SEED, num_seqs: int = 256) -> tuple[list[int], list[int]]:
+    """256 decode rows, total KV length uniform in [1024, 4096]."""
+    g = _gen(seed, 4096, 1)
+    kv = torch.randint(1024, 4096 + 1, (num_seqs,), generator=g).tolist()
+    return [1] * num_seqs, kv
+
+
 WORKLOADS = {
     "correctness": lengths_correctness,
     "chunked_prefill_4k": lengths_chunked_4k,
     "chunked_prefill_16k": lengths_chunked_16k,
     "mixed_256": lengths_mixed,
+    "decode_16k": lengths_decode_16k,
+    "decode_4k": lengths_decode_4k,
 }
+
+
+def attention_kv_bytes(query_lens: Sequence[int], kv_lens: Sequence[int], num_kv_heads: int = 2,
+                       head_dim: int = 128, elem: int = 2, num_q_heads: int = 16) -> int:
+    """Bytes one pass must move at minimum: every K and V row of every sequence once, Q read, O written."""
+    kv = 2 * sum(kv_lens) * num_kv_heads * head_dim * elem
+    qo = 2 * sum(query_lens) * num_q_heads * head_dim * elem
+    return kv + qo
 
 
 def correctness_batch(seed: int = DEFAULT_SEED, dtype: torch.dtype = torch.bfloat16) -> AttentionBatch:

@@ -123,7 +123,7 @@ int decode_chunk(int num_seqs, int hkv, int max_k, int num_sms) {
 }
 
 struct DecodeLayout {
-  size_t base_off, m_off, l_off, o_off, total;
+  size_t base_off, order_off, m_off, l_off, o_off, total;
   int chunk;
   int64_t items_ub;
 };
@@ -133,7 +133,8 @@ DecodeLayout decode_layout(int num_seqs, int hkv, int group, int max_k, int num_
   d.chunk = decode_chunk(num_seqs, hkv, max_k, num_sms);
   d.items_ub = (int64_t)num_seqs * hkv * ((std::max(max_k, 0) + d.chunk - 1) / d.chunk);
   d.base_off = 0;
-  d.m_off = align_up(sizeof(int) * (size_t)(num_seqs + 1), 256);
+  d.order_off = align_up(sizeof(int) * (size_t)(num_seqs + 2), 256);
+  d.m_off = align_up(d.order_off + sizeof(int) * (size_t)d.items_ub, 256);
   d.l_off = align_up(d.m_off + sizeof(float) * (size_t)d.items_ub * group, 256);
   d.o_off = align_up(d.l_off + sizeof(float) * (size_t)d.items_ub * group, 256);
   d.total = align_up(d.o_off + sizeof(float) * (size_t)d.items_ub * group * b200::kAttnHeadDim, 256);
@@ -208,6 +209,7 @@ int run_decode(const B200AttnParams* p, cudaStream_t s, int group) {
   a.cu_q = p->cu_seqlens_q;
   a.seqused = p->seqused_k;
   a.item_base = reinterpret_cast<int*>(ws + dl.base_off);
+  a.order = reinterpret_cast<int*>(ws + dl.order_off);
   a.part_m = reinterpret_cast<float*>(ws + dl.m_off);
   a.part_l = reinterpret_cast<float*>(ws + dl.l_off);
   a.part_o = reinterpret_cast<float*>(ws + dl.o_off);
@@ -225,13 +227,32 @@ int run_decode(const B200AttnParams* p, cudaStream_t s, int group) {
   b200::decode_schedule_kernel<<<1, b200::kSchedThreads, 0, s>>>(a);
   if (int r = check_launch("decode_schedule_kernel")) return r;
   const dim3 grid((unsigned)std::min<int64_t>(sms, dl.items_ub));
+  // The decode and combine kernels are launched as programmatic dependents of
+  // their predecessor: each starts while the previous grid finishes and waits
+  // for it (griddepcontrol.wait) before reading its output.
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
   auto launch = [&](auto kernel) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kDecodeSmemAlloc);
-    kernel<<<grid, b200::kDecThreads, b200::kDecodeSmemAlloc, s>>>(tm_q, maps, a);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(b200::kDecThreads);
+    cfg.dynamicSmemBytes = b200::kDecodeSmemAlloc;
+    cfg.stream = s;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, tm_q, maps, a);
   };
   auto launch_combine = [&](auto kernel) {
     const int64_t warps = (int64_t)p->num_seqs * p->num_q_heads;
-    kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a, p->out, p->out_stride_t, p->out_stride_h, p->num_q_heads);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((warps + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, a, p->out, p->out_stride_t, p->out_stride_h, p->num_q_heads);
   };
 #define B200_DECODE_G(T)                                                                          \
   switch (group) {                                                                                \

@@ -8,10 +8,13 @@
 //
 // Decode streams every K/V row once for only G query rows per KV head, so the
 // bound is HBM bandwidth and the layout is chosen for it:
-//   * work item = (sequence, KV head, chunk of C keys); persistent CTAs take
-//     items round-robin, so the K/V ring keeps streaming across item
-//     boundaries; each item leaves a partial (unnormalised O, m, l) that
-//     decode_combine_kernel merges per (sequence, query head);
+//   * work item = (sequence, KV head, chunk of C keys); the schedule kernel
+//     lists the items longest first and persistent CTAs claim them from a
+//     global counter (the producer of K claims, and hands the item to the
+//     other warps through a 4-entry ring in shared memory), so the CTAs end
+//     within about one item of each other and the K/V rings keep streaming
+//     across item boundaries; each item leaves a partial (unnormalised O, m, l)
+//     that decode_combine_kernel merges per (sequence, query head);
 //   * the UMMAs put the keys on M: S^T = K_j Q^T (M = 128 keys, N = 16 query
 //     heads of the group padded with zero rows, K = head_dim), and
 //     O^T += V_j^T P^T (M = head_dim, N = 16, K = 128 keys; V^T is the V tile
@@ -51,8 +54,10 @@ constexpr uint32_t kDsP = 8192;                             // 2 x 4 KB: two key
 constexpr uint32_t kDsK = 16384;                            // K ring
 constexpr uint32_t kDsV = kDsK + kDecStages * 32768;        // V ring
 constexpr uint32_t kDsRed = kDsV + kDecStages * 32768;      // 2 x 4 x 16 floats (max), 4 x 16 floats (sum)
+constexpr uint32_t kDsItems = kDsRed + 768;                 // ring of claimed item indices
+constexpr int kDecItemRing = 4;
 constexpr uint32_t kDsBar = kDsRed + 1024;
-constexpr uint32_t kDsBytes = kDsBar + 256;
+constexpr uint32_t kDsBytes = kDsBar + 512;
 constexpr uint32_t kDecodeSmemAlloc = kDsBytes + 1024;
 
 enum : int {
@@ -68,16 +73,19 @@ enum : int {
   DB_O_FREE = DB_P_EMPTY + 2,            // + buffer, 4 arrivals
   DB_RED = DB_O_FREE + 2,                // + buffer, 4 arrivals
   DB_LRED = DB_RED + 2,                  // 4 arrivals
-  DB_DRAIN = DB_LRED + 1,
+  DB_IT_FULL = DB_LRED + 1,              // + ring entry
+  DB_IT_EMPTY = DB_IT_FULL + kDecItemRing,  // + ring entry, 6 arrivals (V producer, UMMA, 4 softmax warps)
+  DB_DRAIN = DB_IT_EMPTY + kDecItemRing,
   DB_COUNT = DB_DRAIN + 1
 };
-static_assert(DB_COUNT * 8 + 8 <= 256, "barrier area");
+static_assert(DB_COUNT * 8 + 8 <= 512, "barrier area");
 
 struct DecodeArgs {
   const void* block_table;
   const void* cu_q;
   const void* seqused;
-  int* item_base;  // [num_seqs + 1], written by decode_schedule_kernel
+  int* item_base;  // [num_seqs + 2]: first item of each sequence, total, claim counter
+  int* order;      // [items]: item indices, longest first
   float* part_o;   // [items][G][128], unnormalised
   float* part_m;   // [items][G], running maximum in scaled base-2 units
   float* part_l;   // [items][G]
@@ -118,9 +126,16 @@ __device__ __forceinline__ DecodeItem decode_item(const DecodeArgs& a, int item)
 }
 
 // Items per sequence (KH x chunks of its keys; none unless it has exactly one
-// query token and at least one key), exclusive prefix into item_base.
+// query token and at least one key), exclusive prefix into item_base; then the
+// item list ordered by tile count, longest first (bucket sort), and the claim
+// counter reset.
 __global__ void __launch_bounds__(kSchedThreads, 1) decode_schedule_kernel(const DecodeArgs a) {
   __shared__ int warp_sums[32];
+  __shared__ int hist[kSchedBuckets];
+  __shared__ int s_total;
+  // The decode kernel may launch now: it sets itself up and then waits for
+  // this grid before it reads the item list.
+  griddep_launch_dependents();
   int carry = 0;
   for (int base = 0; base < a.num_seqs; base += kSchedThreads) {
     const int b = base + threadIdx.x;
@@ -136,7 +151,36 @@ __global__ void __launch_bounds__(kSchedThreads, 1) decode_schedule_kernel(const
     if (b < a.num_seqs) a.item_base[b] = carry + before;
     carry += total;
   }
-  if (threadIdx.x == 0) a.item_base[a.num_seqs] = carry;
+  if (threadIdx.x == 0) {
+    a.item_base[a.num_seqs] = carry;
+    a.item_base[a.num_seqs + 1] = 0;
+    s_total = carry;
+  }
+  for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;
+  __syncthreads();
+  const int total = s_total;
+  auto bucket_of = [&](int item) { return min(decode_item(a, item).n_tiles, kSchedBuckets - 1); };
+  for (int u = threadIdx.x; u < total; u += kSchedThreads) atomicAdd(&hist[bucket_of(u)], 1);
+  __syncthreads();
+  {
+    constexpr int per = kSchedBuckets / kSchedThreads;
+    int local[per];
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < per; ++k) {
+      local[k] = hist[kSchedBuckets - 1 - (threadIdx.x * per + k)];
+      sum += local[k];
+    }
+    int all;
+    int before = block_exclusive_scan(sum, warp_sums, all);
+#pragma unroll
+    for (int k = 0; k < per; ++k) {
+      hist[kSchedBuckets - 1 - (threadIdx.x * per + k)] = before;
+      before += local[k];
+    }
+  }
+  __syncthreads();
+  for (int u = threadIdx.x; u < total; u += kSchedThreads) a.order[atomicAdd(&hist[bucket_of(u)], 1)] = u;
 }
 
 // Byte offset of element (row, col) of a [16 x 128] bf16/f16 operand stored
@@ -170,9 +214,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                         const DecodeArgs a) {
   static_assert(G >= 1 && G <= kDecN, "query heads per KV head");
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  const int total = a.item_base[a.num_seqs];
-  if (static_cast<int>(blockIdx.x) >= total) return;
-
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_addr(smem);
@@ -180,7 +221,19 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kDsBar + DB_COUNT * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kDsBar + DB_COUNT * 8 + 4);
   float* red = reinterpret_cast<float*>(smem + kDsRed);  // [2][4][16] maxima, then [4][16] sums
+  volatile int* item_ring = reinterpret_cast<volatile int*>(smem + kDsItems);
   auto bar = [&](int i) { return smem_addr(&bars[i]); };
+  // Item n of this CTA, as claimed by the K producer; -1 ends the loop (also
+  // on abort).  One thread per warp waits; the warp reads the broadcast.
+  auto pop_item = [&](int n) -> int {
+    int item = -1;
+    if ((threadIdx.x & 31) == 0) {
+      const int e = n % kDecItemRing;
+      if (mbar_wait(bar(DB_IT_FULL + e), (n / kDecItemRing) & 1, abort_flag)) item = item_ring[e];
+      mbar_arrive(bar(DB_IT_EMPTY + e));
+    }
+    return __shfl_sync(0xffffffffu, item, 0);
+  };
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
@@ -201,6 +254,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       mbar_init(bar(DB_V_EMPTY + s), 1);
     }
     mbar_init(bar(DB_LRED), 4);
+    for (int e = 0; e < kDecItemRing; ++e) {
+      mbar_init(bar(DB_IT_FULL + e), 1);
+      mbar_init(bar(DB_IT_EMPTY + e), 6);
+    }
     mbar_init(bar(DB_DRAIN), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -216,6 +273,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Set-up done; the item list of the schedule kernel is needed from here on.
+  griddep_wait();
+  const int total = a.item_base[a.num_seqs];
 
   if (warp == 0 || warp == 2) {
     // ------------------------------------------------------------ producers (whole warps)
@@ -240,8 +300,33 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     };
     int fills = 0, q_uses0 = 0, q_uses1 = 0;
     bool ok = true;
-    int it = 0;
-    for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++it) {
+    int* counter = a.item_base + a.num_seqs + 1;
+    int claimed = -1;
+    if (is_k && lane == 0) {
+      const int k = atomicAdd(counter, 1);
+      claimed = k < total ? a.order[k] : -1;
+    }
+    for (int it = 0; ok; ++it) {
+      int item;
+      if (is_k) {
+        // Publish the claimed item to the other warps, then claim the next one
+        // (its latency overlaps this item's copies).
+        int okr = 1;
+        if (lane == 0) {
+          const int e = it % kDecItemRing;
+          okr = mbar_wait(bar(DB_IT_EMPTY + e), ((it / kDecItemRing) & 1) ^ 1, abort_flag);
+          item_ring[e] = okr ? claimed : -1;
+          mbar_arrive(bar(DB_IT_FULL + e));
+        }
+        item = __shfl_sync(0xffffffffu, okr ? claimed : -1, 0);
+        if (item >= 0 && lane == 0) {
+          const int k = atomicAdd(counter, 1);
+          claimed = k < total ? a.order[k] : -1;
+        }
+      } else {
+        item = pop_item(it);
+      }
+      if (item < 0) break;
       const DecodeItem d = decode_item(a, item);
       const CUtensorMap* map = is_k ? &maps.k[d.kvh] : &maps.v[d.kvh];
       int pg_cur, of_cur, pg_nxt = a.num_blocks, of_nxt = 0;
@@ -318,9 +403,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         tc_commit(bar(DB_P_EMPTY + (p.tile & 1)));
         return true;
       };
-      int tile = 0, it = 0;  // tile = index of the K fill and of the V fill
+      int tile = 0;  // tile = index of the K fill and of the V fill
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++it) {
+      for (int it = 0; ok; ++it) {
+        int item = -1;
+        {
+          const int e = it % kDecItemRing;
+          if (mbar_wait(bar(DB_IT_FULL + e), (it / kDecItemRing) & 1, abort_flag)) item = item_ring[e];
+          mbar_arrive(bar(DB_IT_EMPTY + e));
+        }
+        if (item < 0) break;
         const DecodeItem d = decode_item(a, item);
         const int qb = it & 1;
         if (!mbar_wait(bar(DB_Q_FULL + qb), (it >> 1) & 1, abort_flag)) break;
@@ -346,9 +438,18 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             break;
           }
           pend = Pending{vidx, it, tile, j == 0, true};
+          // The item's last P^T V goes out at once: its epilogue waits for it,
+          // and nothing of the next item may overtake it.
+          if (j + 1 == d.n_tiles) {
+            if (!issue_pv(pend)) {
+              ok = false;
+              break;
+            }
+            pend.valid = false;
+          }
         }
       }
-      if (ok && pend.valid) issue_pv(pend);
+
       tc_commit(bar(DB_DRAIN));
       mbar_wait_drain(bar(DB_DRAIN), 0);
     }
@@ -362,9 +463,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const int r = quarter * 32 + lane;  // key row of S^T; row d of O^T
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = a.scale_log2;
-    int tile = 0, it = 0;
+    int tile = 0;
     bool aborted = false;
-    for (int item = blockIdx.x; !aborted && item < total; item += gridDim.x, ++it) {
+    for (int it = 0; !aborted; ++it) {
+      const int item = pop_item(it);
+      if (item < 0) break;
       const DecodeItem d = decode_item(a, item);
       float m_used[G], l_thr[G];
 #pragma unroll
@@ -525,6 +628,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  griddep_launch_dependents();  // the combine may launch; it waits for this grid to end
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kDecTmemCols);
@@ -537,6 +641,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 template <typename T, int G>
 __global__ void __launch_bounds__(256) decode_combine_kernel(const DecodeArgs a, void* out, int64_t out_st,
                                                              int64_t out_sh, int num_q_heads) {
+  griddep_wait();  // the partials of the decode kernel
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= a.num_seqs * num_q_heads) return;

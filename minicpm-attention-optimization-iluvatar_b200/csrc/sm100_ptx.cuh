@@ -115,6 +115,13 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* map, uint3
       : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start before its predecessor ends; griddep_wait blocks
+// until the predecessor grid has completed and its memory is visible, and
+// griddep_launch_dependents lets the next kernel start launching.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Generic-proxy shared-memory writes -> visible to the async proxy (UMMA reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

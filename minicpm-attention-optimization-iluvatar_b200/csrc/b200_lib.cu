@@ -472,7 +472,19 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
                   b200::kAttnLaunchRegs);
     const uint32_t smem = pair ? b200::kAttnPairSmemAlloc : b200::kAttnSmemAlloc;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    kernel<<<grid, b200::kAttnThreads, smem, s>>>(tm_q, tm_k, tm_v, a);
+    // A programmatic dependent of the schedule kernel: launched while it runs,
+    // it waits for it (griddepcontrol.wait) before reading the work list.
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(b200::kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, tm_q, tm_k, tm_v, a);
     return B200_OK;
   };
   int lr;

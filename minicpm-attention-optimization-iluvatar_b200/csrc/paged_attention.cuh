@@ -175,6 +175,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     paged_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const AttnKernelArgs a) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  griddep_wait();  // launched as a programmatic dependent of the schedule kernel
   if (static_cast<int>(blockIdx.x) >= *a.unit_count) return;
 
   extern __shared__ uint8_t smem_raw[];
@@ -609,6 +610,7 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   __shared__ int hist[kSchedBuckets];
   __shared__ int warp_sums[32];
   __shared__ int s_total_tiles;
+  griddep_launch_dependents();  // the attention grid may launch; it waits for this one
 
   // 1. query tiles per sequence, exclusive prefix over sequences.
   int carry = 0;

@@ -57,6 +57,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kAttnThreads, 1)
                                const __grid_constant__ CUtensorMap tm_v, const AttnKernelArgs a) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  griddep_wait();  // launched as a programmatic dependent of the schedule kernel
   if (cluster_id >= *a.unit_count) return;  // uniform across the pair
 
   extern __shared__ uint8_t smem_raw[];

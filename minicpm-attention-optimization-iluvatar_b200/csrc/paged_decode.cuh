@@ -54,7 +54,7 @@ constexpr uint32_t kDsP = 8192;                             // 2 x 4 KB: two key
 constexpr uint32_t kDsK = 16384;                            // K ring
 constexpr uint32_t kDsV = kDsK + kDecStages * 32768;        // V ring
 constexpr uint32_t kDsRed = kDsV + kDecStages * 32768;      // 2 x 4 x 16 floats (max), 4 x 16 floats (sum)
-constexpr uint32_t kDsItems = kDsRed + 768;                 // ring of claimed item indices
+constexpr uint32_t kDsItems = kDsRed + 768;                 // ring of claimed items (8 ints each)
 constexpr int kDecItemRing = 4;
 constexpr uint32_t kDsBar = kDsRed + 1024;
 constexpr uint32_t kDsBytes = kDsBar + 512;
@@ -107,17 +107,18 @@ struct DecodeItem {
   int seq, kvh, kv_begin, kv_end, L, n_tiles;
 };
 
-__device__ __forceinline__ DecodeItem decode_item(const DecodeArgs& a, int item) {
+// `base` is item_base (global memory) or a copy of it in shared memory.
+__device__ __forceinline__ DecodeItem decode_item(const DecodeArgs& a, const int* base, int item) {
   int lo = 0, hi = a.num_seqs - 1;  // last sequence whose first item is <= item
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (a.item_base[mid] <= item) lo = mid; else hi = mid - 1;
+    if (base[mid] <= item) lo = mid; else hi = mid - 1;
   }
   DecodeItem d;
   d.seq = lo;
   d.L = load_index(a.seqused, lo, a.len_i64);
   const int chunks = (d.L + a.chunk - 1) / a.chunk;
-  const int rem = item - a.item_base[lo];
+  const int rem = item - base[lo];
   d.kvh = rem / chunks;
   d.kv_begin = (rem - d.kvh * chunks) * a.chunk;
   d.kv_end = min(d.kv_begin + a.chunk, d.L);
@@ -129,10 +130,14 @@ __device__ __forceinline__ DecodeItem decode_item(const DecodeArgs& a, int item)
 // query token and at least one key), exclusive prefix into item_base; then the
 // item list ordered by tile count, longest first (bucket sort), and the claim
 // counter reset.
+constexpr int kDecSchedSmemSeqs = 4096;  // item_base kept in shared memory up to this many sequences
+
 __global__ void __launch_bounds__(kSchedThreads, 1) decode_schedule_kernel(const DecodeArgs a) {
   __shared__ int warp_sums[32];
   __shared__ int hist[kSchedBuckets];
+  __shared__ int s_base[kDecSchedSmemSeqs + 1];
   __shared__ int s_total;
+  const bool in_smem = a.num_seqs <= kDecSchedSmemSeqs;
   // The decode kernel may launch now: it sets itself up and then waits for
   // this grid before it reads the item list.
   griddep_launch_dependents();
@@ -148,7 +153,10 @@ __global__ void __launch_bounds__(kSchedThreads, 1) decode_schedule_kernel(const
     }
     int total;
     const int before = block_exclusive_scan(n, warp_sums, total);
-    if (b < a.num_seqs) a.item_base[b] = carry + before;
+    if (b < a.num_seqs) {
+      a.item_base[b] = carry + before;
+      if (in_smem) s_base[b] = carry + before;
+    }
     carry += total;
   }
   if (threadIdx.x == 0) {
@@ -159,7 +167,8 @@ __global__ void __launch_bounds__(kSchedThreads, 1) decode_schedule_kernel(const
   for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;
   __syncthreads();
   const int total = s_total;
-  auto bucket_of = [&](int item) { return min(decode_item(a, item).n_tiles, kSchedBuckets - 1); };
+  const int* base = in_smem ? s_base : a.item_base;
+  auto bucket_of = [&](int item) { return min(decode_item(a, base, item).n_tiles, kSchedBuckets - 1); };
   for (int u = threadIdx.x; u < total; u += kSchedThreads) atomicAdd(&hist[bucket_of(u)], 1);
   __syncthreads();
   {
@@ -221,18 +230,27 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kDsBar + DB_COUNT * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kDsBar + DB_COUNT * 8 + 4);
   float* red = reinterpret_cast<float*>(smem + kDsRed);  // [2][4][16] maxima, then [4][16] sums
+  // Ring entry: {item, seq, kvh, kv_begin, kv_end, L, n_tiles, -}.
   volatile int* item_ring = reinterpret_cast<volatile int*>(smem + kDsItems);
   auto bar = [&](int i) { return smem_addr(&bars[i]); };
-  // Item n of this CTA, as claimed by the K producer; -1 ends the loop (also
-  // on abort).  One thread per warp waits; the warp reads the broadcast.
-  auto pop_item = [&](int n) -> int {
-    int item = -1;
-    if ((threadIdx.x & 31) == 0) {
-      const int e = n % kDecItemRing;
-      if (mbar_wait(bar(DB_IT_FULL + e), (n / kDecItemRing) & 1, abort_flag)) item = item_ring[e];
-      mbar_arrive(bar(DB_IT_EMPTY + e));
-    }
-    return __shfl_sync(0xffffffffu, item, 0);
+  // Item n of this CTA, as claimed and decoded by the K producer; -1 ends the
+  // loop (also on abort).  Lane 0 waits; the warp reads the entry.
+  auto pop_item = [&](int n, DecodeItem& d) -> int {
+    const int e = n % kDecItemRing;
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar(DB_IT_FULL + e), (n / kDecItemRing) & 1, abort_flag);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    const volatile int* en = item_ring + 8 * e;
+    const int item = ok ? en[0] : -1;
+    d.seq = en[1];
+    d.kvh = en[2];
+    d.kv_begin = en[3];
+    d.kv_end = en[4];
+    d.L = en[5];
+    d.n_tiles = en[6];
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar(DB_IT_EMPTY + e));
+    return item;
   };
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -308,26 +326,40 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
     for (int it = 0; ok; ++it) {
       int item;
+      DecodeItem d{};
       if (is_k) {
-        // Publish the claimed item to the other warps, then claim the next one
-        // (its latency overlaps this item's copies).
+        // Decode and publish the claimed item to the other warps, then claim
+        // the next one (its latency overlaps this item's copies).
         int okr = 1;
         if (lane == 0) {
           const int e = it % kDecItemRing;
           okr = mbar_wait(bar(DB_IT_EMPTY + e), ((it / kDecItemRing) & 1) ^ 1, abort_flag);
-          item_ring[e] = okr ? claimed : -1;
+          if (okr && claimed >= 0) d = decode_item(a, a.item_base, claimed);
+          volatile int* en = item_ring + 8 * e;
+          en[0] = okr ? claimed : -1;
+          en[1] = d.seq;
+          en[2] = d.kvh;
+          en[3] = d.kv_begin;
+          en[4] = d.kv_end;
+          en[5] = d.L;
+          en[6] = d.n_tiles;
           mbar_arrive(bar(DB_IT_FULL + e));
         }
         item = __shfl_sync(0xffffffffu, okr ? claimed : -1, 0);
+        d.seq = __shfl_sync(0xffffffffu, d.seq, 0);
+        d.kvh = __shfl_sync(0xffffffffu, d.kvh, 0);
+        d.kv_begin = __shfl_sync(0xffffffffu, d.kv_begin, 0);
+        d.kv_end = __shfl_sync(0xffffffffu, d.kv_end, 0);
+        d.L = __shfl_sync(0xffffffffu, d.L, 0);
+        d.n_tiles = __shfl_sync(0xffffffffu, d.n_tiles, 0);
         if (item >= 0 && lane == 0) {
           const int k = atomicAdd(counter, 1);
           claimed = k < total ? a.order[k] : -1;
         }
       } else {
-        item = pop_item(it);
+        item = pop_item(it, d);
       }
       if (item < 0) break;
-      const DecodeItem d = decode_item(a, item);
       const CUtensorMap* map = is_k ? &maps.k[d.kvh] : &maps.v[d.kvh];
       int pg_cur, of_cur, pg_nxt = a.num_blocks, of_nxt = 0;
       lookup(d, 0, pg_cur, of_cur);
@@ -407,13 +439,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       bool ok = true;
       for (int it = 0; ok; ++it) {
         int item = -1;
+        DecodeItem d{};
         {
           const int e = it % kDecItemRing;
-          if (mbar_wait(bar(DB_IT_FULL + e), (it / kDecItemRing) & 1, abort_flag)) item = item_ring[e];
+          if (mbar_wait(bar(DB_IT_FULL + e), (it / kDecItemRing) & 1, abort_flag)) item = item_ring[8 * e];
+          d.n_tiles = item_ring[8 * e + 6];
           mbar_arrive(bar(DB_IT_EMPTY + e));
         }
         if (item < 0) break;
-        const DecodeItem d = decode_item(a, item);
         const int qb = it & 1;
         if (!mbar_wait(bar(DB_Q_FULL + qb), (it >> 1) & 1, abort_flag)) break;
         for (int j = 0; j < d.n_tiles; ++j, ++tile) {
@@ -466,9 +499,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     int tile = 0;
     bool aborted = false;
     for (int it = 0; !aborted; ++it) {
-      const int item = pop_item(it);
+      DecodeItem d{};
+      const int item = pop_item(it, d);
       if (item < 0) break;
-      const DecodeItem d = decode_item(a, item);
       float m_used[G], l_thr[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) {

@@ -686,18 +686,36 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const DecodeArgs a,
   const int kvh = h / G, g = h - kvh * G;
   float acc[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.f;
   if (chunks > 0) {
+    // m and l of up to 32 chunks in one round of loads across the lanes, then
+    // the O rows eight chunks at a time, so the loads overlap.
     const int first = a.item_base[b] + kvh * chunks;
     float mmax = -INFINITY;
-    for (int c = 0; c < chunks; ++c) mmax = fmaxf(mmax, a.part_m[static_cast<int64_t>(first + c) * G + g]);
-    for (int c = 0; c < chunks; ++c) {
+    for (int c = lane; c < chunks; c += 32) mmax = fmaxf(mmax, a.part_m[static_cast<int64_t>(first + c) * G + g]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, off));
+    for (int c = lane; c < chunks; c += 32) {
       const int64_t row = static_cast<int64_t>(first + c) * G + g;
-      const float wc = ex2_approx(a.part_m[row] - mmax);
-      den += wc * a.part_l[row];
-      const float4 o = reinterpret_cast<const float4*>(a.part_o + row * 128)[lane];
-      acc[0] += wc * o.x;
-      acc[1] += wc * o.y;
-      acc[2] += wc * o.z;
-      acc[3] += wc * o.w;
+      den += ex2_approx(a.part_m[row] - mmax) * a.part_l[row];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+    for (int c0 = 0; c0 < chunks; c0 += 8) {
+      float4 o[8];
+      float w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u;
+        const int64_t row = static_cast<int64_t>(first + min(c, chunks - 1)) * G + g;
+        o[u] = reinterpret_cast<const float4*>(a.part_o + row * 128)[lane];
+        w[u] = c < chunks ? ex2_approx(a.part_m[row] - mmax) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        acc[0] += w[u] * o[u].x;
+        acc[1] += w[u] * o[u].y;
+        acc[2] += w[u] * o[u].z;
+        acc[3] += w[u] * o[u].w;
+      }
     }
   }
   const float inv = 1.f / fmaxf(den, 1e-20f);

@@ -61,6 +61,8 @@ def parse_args():
     ap.add_argument("--service", action="store_true",
                     help="rope_16384: the service's rope-and-cache call (key rotated in place)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="attention workloads: time the K calls as one CUDA graph replay (no host launch gaps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--verify", action="store_true", help="gather outputs to rank 0 (NCCL) and check sampled rows")
     return ap.parse_args()
@@ -533,20 +535,41 @@ def attention_bench(args, world, rank, local):
     barrier(world)
     stream = torch.cuda.current_stream(dev)
     per_launch = []
+    if args.graph:
+        # The K calls captured in one CUDA graph (as a serving engine replays
+        # its decode steps) and replayed once inside the events.
+        gstream = torch.cuda.Stream(device=dev)
+        gstream.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(gstream):
+            with torch.cuda.graph(graph, stream=gstream):
+                for _ in range(args.steps):
+                    step()
+        stream.wait_stream(gstream)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        barrier(world)
     with ClockSampler(dev.index) as clocks:
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         start.record(stream)
-        for s, e in evs:
-            s.record(stream)
-            step()
-            e.record(stream)
+        if args.graph:
+            graph.replay()
+        else:
+            for s, e in evs:
+                s.record(stream)
+                step()
+                e.record(stream)
         end.record(stream)
         end.synchronize()
     barrier(world)
     elapsed_ms = start.elapsed_time(end)
-    per_launch = [s.elapsed_time(e) for s, e in evs]
+    if args.graph:
+        per_launch = [elapsed_ms / args.steps] * args.steps
+        del graph
+    else:
+        per_launch = [s.elapsed_time(e) for s, e in evs]
     max_ms = max_over_ranks(elapsed_ms, world)
     value = total_flops * args.steps / (max_ms * 1e-3) / 1e12
     tokens_per_s = total_tokens * args.steps / (max_ms * 1e-3)
@@ -647,6 +670,7 @@ def attention_bench(args, world, rank, local):
             "heads": "16q/2kv", "head_dim": 128, "page_size": 16,
             "num_splits": resolved,
             "parallelism": f"sequence-sharded x{world}",
+            "timing": "one CUDA graph of the K calls" if args.graph else "K calls launched from Python",
             "l2": l2_note,
         },
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",

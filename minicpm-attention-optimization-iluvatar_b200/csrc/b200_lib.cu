@@ -379,6 +379,9 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
         p->v_stride_tok | p->v_stride_head | p->out_stride_t | p->out_stride_h) *
        elt) & 15)
     return fail(B200_ERR_UNSUPPORTED, "token/head/block strides must be multiples of 16 bytes");
+  // Decode batches take the decode kernel (its own workspace layout and maps).
+  if (p->max_seqlen_q == 1 && decode_shape_ok(group, p->num_kv_heads) && use_decode_kernel())
+    return run_decode(p, static_cast<cudaStream_t>(stream), group);
 
   const int splits = p->num_splits > 0 ? p->num_splits
                                        : b200_choose_num_splits(p->total_q, p->num_seqs, p->num_q_heads,
@@ -412,8 +415,6 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   }
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (p->max_seqlen_q == 1 && decode_shape_ok(group, p->num_kv_heads) && use_decode_kernel())
-    return run_decode(p, s, group);
   // CTA-pair kernel (M = 256 UMMA across two SMs) or single-CTA kernel.
   const bool pair = use_cta_pair();
   const int units_per_tile_group = pair ? b200::kPairTilesPerUnit : b200::kAttnTilesPerUnit;

@@ -80,6 +80,34 @@ def test_plain_cache_write(dtype, kh, d, slot_dtype):
     _check_write(b, _run_write(b))
 
 
+@pytest.mark.parametrize("kind", ["auto", "fp8", "int8_per_token_head"])
+def test_padded_token_rows(kind):
+    """key / value rows with padding after each token (token stride > heads x head_dim)."""
+    b = build_kv_write_batch(777, kv_cache_dtype=kind, num_blocks=64, padding_tokens=5)
+    want = _want(b)
+    g = b.to("cuda")
+    t, kh, d = b.key.shape
+    pad_k = torch.zeros(t, kh * d + 64, dtype=b.key.dtype, device="cuda")
+    pad_v = torch.zeros_like(pad_k)
+    pad_k[:, : kh * d] = g.key.reshape(t, -1)
+    pad_v[:, : kh * d] = g.value.reshape(t, -1)
+    key = pad_k[:, : kh * d].view(t, kh, d)
+    value = pad_v[:, : kh * d].view(t, kh, d)
+    assert key.stride(0) == kh * d + 64
+    kc, vc = g.caches()
+    if kind.endswith("per_token_head"):
+        ks, vs = g.scale_cache_views()
+        kv_cache.reshape_and_cache_flash_per_token_head_quant(key, value, kc, vc, ks, vs, g.slot_mapping)
+    else:
+        kv_cache.reshape_and_cache_flash(key, value, kc, vc, g.slot_mapping, kind, g.k_scale, g.v_scale)
+    torch.cuda.synchronize()
+    assert torch.equal(_u8(kc), _u8(want[0])) and torch.equal(_u8(vc), _u8(want[1]))
+    if want[2] is not None:
+        ks, vs = g.scale_cache_views()
+        assert torch.equal(ks.cpu(), want[2]) and torch.equal(vs.cpu(), want[3])
+    assert _lib.device_error() == _lib.DEVERR_NONE
+
+
 @pytest.mark.parametrize("storage", [torch.float8_e4m3fn, torch.uint8])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_fp8_per_tensor_cache_write(storage, dtype):

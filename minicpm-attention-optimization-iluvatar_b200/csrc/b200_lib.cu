@@ -458,11 +458,13 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   a.num_splits = splits;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
-  // Upper bound on work units for this unit size; surplus CTAs exit at once.
+  // Upper bound on work units for this unit size (surplus CTAs of the pair
+  // kernel exit at once).
   const int64_t units_ub =
       ((int64_t)p->total_q + sa.pos_per_unit - 1) / sa.pos_per_unit + p->num_seqs;
   const int64_t ctas = units_ub * p->num_kv_heads * splits * (pair ? 2 : 1);
-  const dim3 grid(static_cast<unsigned>(ctas));
+  // The single-CTA kernel is persistent: one CTA per SM at most.
+  const dim3 grid(static_cast<unsigned>(pair ? ctas : std::min<int64_t>(ctas, sm_count())));
   auto launch = [&](auto kernel) -> int {
     // The kernel rebalances registers between warpgroups with setmaxnreg; the
     // split adds up only if every thread was launched with exactly

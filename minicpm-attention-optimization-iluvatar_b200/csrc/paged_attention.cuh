@@ -17,12 +17,18 @@
 // holds two such tiles (2P consecutive positions, 256 rows) that share every
 // K/V tile; the second is skipped when the sequence has no rows for it.
 //
-// One CTA per unit, 12 warps in 3 warpgroups:
-//   warp 0      TMA producer: Q0/Q1 once, then K_j and V_j tiles of 128 tokens
-//               into a 5-slot ring, each tile as 8 page slices of 16 tokens x
-//               2 half-rows (a per-page gather through the block table).
-//               Slices past the unit's last key use an out-of-range page
-//               index, so TMA fills zeros and reads nothing outside the cache.
+// Persistent CTAs, one per SM, each looping over units that it claims from
+// the heaviest-first work list (attn_schedule_kernel) with an atomic counter;
+// 12 warps in 3 warpgroups:
+//   warp 0      producer: claims a unit and publishes it in a 4-entry
+//               shared-memory ring, then issues the TMA copies: Q0/Q1 once
+//               the previous unit's last S is issued (Q_EMPTY), then K_j and
+//               V_j tiles of 128 tokens into a 5-slot ring, each tile as 8
+//               page slices of 16 tokens x 2 half-rows (a per-page gather
+//               through the block table).  Slices past the unit's last key
+//               use an out-of-range page index, so TMA fills zeros and reads
+//               nothing outside the cache.  The next unit's copies therefore
+//               overlap the current unit's last tiles and epilogue.
 //   warp 1      TMEM owner and single-thread UMMA issuer, in the order
 //               S0(j+1) = Q0 K^T after PV0(j), S1(j+1) after PV1(j), so each
 //               softmax warpgroup works while the tensor core runs the other
@@ -34,6 +40,10 @@
 //               running maximum is raised only when a row maximum grows by
 //               more than 2^8; only then is O rescaled (rare after the first
 //               tile).  Final normalise and store.
+// Barrier phases run on counters kept across units: K/V ring fills, Q loads,
+// and tiles per query tile (S_FULL, P_FULL, O_DONE).  A unit's first PV
+// overwrites O_t only after tile t's softmax warps have published its first
+// P, which they do after their epilogue has read the previous unit's O_t.
 // TMEM: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512); P_t in the
 // first 64 columns of S_t.
 // Registers: launched at 168 per thread (the 384-thread limit); the first
@@ -67,21 +77,33 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
 // Shared memory map (offsets from a 1024-aligned base).
 constexpr uint32_t kSmQ = 0;                            // Q0, Q1: 2 x (2 x 16 KB)
 constexpr uint32_t kSmKV = 65536;                       // ring: kKvStages x 32 KB
-constexpr uint32_t kSmBar = kSmKV + kKvStages * 32768;  // mbarriers
-constexpr uint32_t kSmBytes = kSmBar + 256;
+constexpr uint32_t kSmBar = kSmKV + kKvStages * 32768;  // mbarriers, TMEM slot, abort flag, unit ring
+constexpr uint32_t kSmBytes = kSmBar + 512;
 constexpr uint32_t kAttnSmemAlloc = kSmBytes + 1024;    // + alignment slack
+static_assert(kAttnSmemAlloc <= 232448, "shared memory per CTA");
+constexpr int kUnitRing = 4;  // claimed work units in flight between the producer and the consumers
 
 enum : int {
-  BAR_Q = 0,
-  BAR_KV_FULL = 1,                           // + slot
+  BAR_Q_FULL = 0,
+  BAR_Q_EMPTY = 1,
+  BAR_KV_FULL = 2,                           // + slot
   BAR_KV_EMPTY = BAR_KV_FULL + kKvStages,    // + slot
   BAR_S_FULL = BAR_KV_EMPTY + kKvStages,     // + tile
   BAR_P_FULL = BAR_S_FULL + 2,               // + 4 * tile + quarter (32 keys of P)
   BAR_O_DONE = BAR_P_FULL + 8,               // + tile
-  BAR_DRAIN = BAR_O_DONE + 2,
+  BAR_IT_FULL = BAR_O_DONE + 2,              // + ring entry
+  BAR_IT_EMPTY = BAR_IT_FULL + kUnitRing,    // + ring entry
+  BAR_DRAIN = BAR_IT_EMPTY + kUnitRing,
   BAR_COUNT = BAR_DRAIN + 1
 };
-static_assert(BAR_COUNT * 8 + 8 <= 256, "barrier area");
+
+// A claimed unit as the producer publishes it: (seq, qunit, kvh, split),
+// then cu_q[seq], cu_q[seq + 1], seqused[seq] and a valid flag (0 ends the loop).
+struct UnitEntry {
+  int seq, qunit, kvh, split, q_begin, q_end, seq_len, valid;
+};
+constexpr uint32_t kSmRing = BAR_COUNT * 8 + 16;  // after the barriers, the TMEM slot and the abort flag
+static_assert(kSmRing + kUnitRing * sizeof(UnitEntry) <= 512, "barrier area");
 
 struct AttnKernelArgs {
   const void* block_table;
@@ -176,7 +198,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                           const __grid_constant__ CUtensorMap tm_v, const AttnKernelArgs a) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   griddep_wait();  // launched as a programmatic dependent of the schedule kernel
-  if (static_cast<int>(blockIdx.x) >= *a.unit_count) return;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -184,22 +205,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmBar + BAR_COUNT * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmBar + BAR_COUNT * 8 + 4);
+  volatile UnitEntry* ring = reinterpret_cast<volatile UnitEntry*>(smem + kSmBar + kSmRing);
   auto bar = [&](int i) { return smem_addr(&bars[i]); };
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int P = a.pos_per_tile;
-
-  const int4 unit = a.units[blockIdx.x];
-  const int seq = unit.x, qunit = unit.y, kvh = unit.z, split = unit.w;
-  const UnitGeom ug = unit_geometry(load_index(a.cu_q, seq, a.len_i64), load_index(a.cu_q, seq + 1, a.len_i64),
-                                    load_index(a.seqused, seq, a.len_i64), qunit, split, kAttnTilesPerUnit * P,
-                                    a.num_splits);
-  const int n_tiles = ug.n_tiles;
-  const bool two = ug.pos0 + P < ug.q_len;  // the second query tile has rows
+  const int ppu = kAttnTilesPerUnit * P;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(BAR_Q), 1);
+    mbar_init(bar(BAR_Q_FULL), 1);
+    mbar_init(bar(BAR_Q_EMPTY), 1);
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(bar(BAR_KV_FULL + s), 1);
       mbar_init(bar(BAR_KV_EMPTY + s), 1);
@@ -208,6 +224,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(bar(BAR_S_FULL + t), 1);
       for (int q = 0; q < 4; ++q) mbar_init(bar(BAR_P_FULL + 4 * t + q), 4);
       mbar_init(bar(BAR_O_DONE + t), 1);
+    }
+    for (int r = 0; r < kUnitRing; ++r) {
+      mbar_init(bar(BAR_IT_FULL + r), 1);
+      mbar_init(bar(BAR_IT_EMPTY + r), 9);  // the MMA issuer and the 8 softmax warps
     }
     mbar_init(bar(BAR_DRAIN), 1);
     *abort_flag = 0;
@@ -222,74 +242,139 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // Consumers read ring entry it; false when the loop must end.
+  auto take_entry = [&](int it, UnitEntry& e) -> bool {
+    const int r = it % kUnitRing;
+    if (!mbar_wait(bar(BAR_IT_FULL + r), (it / kUnitRing) & 1, abort_flag)) return false;
+    e.seq = ring[r].seq;
+    e.qunit = ring[r].qunit;
+    e.kvh = ring[r].kvh;
+    e.split = ring[r].split;
+    e.q_begin = ring[r].q_begin;
+    e.q_end = ring[r].q_end;
+    e.seq_len = ring[r].seq_len;
+    e.valid = ring[r].valid;
+    return true;
+  };
+  auto geometry = [&](const UnitEntry& e) {
+    return unit_geometry(e.q_begin, e.q_end, e.seq_len, e.qunit, e.split, ppu, a.num_splits);
+  };
+
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttnProducerRegs));
-    if (warp == 0 && n_tiles > 0) {
+    if (warp == 0) {
       // ---------------------------------------------------------- producer (whole warp)
-      // Lane c < 8 owns page slice c of a tile: it looks up the slice's physical
-      // page one tile ahead (the block-table reads overlap the previous tile's
-      // copies), and lanes 0..15 each issue one of the tile's 16 TMA boxes.
       if (lane == 0) {
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
-        const int head0 = kvh * a.group;
-        const int t0 = ug.q_begin + ug.pos0;
-        mbar_arrive_expect_tx(bar(BAR_Q), (two ? 2 : 1) * 32768);
-        tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q), 0, head0, t0);
-        tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q), 64, head0, t0);
-        if (two) {
-          tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q), 0, head0, t0 + P);
-          tma_load_3d(sbase + kSmQ + 49152, &tm_q, bar(BAR_Q), 64, head0, t0 + P);
-        }
       }
-      const int64_t bt_row = static_cast<int64_t>(seq) * a.bt_stride;
+      const int unit_count = *a.unit_count;
+      int* claim = const_cast<int*>(a.unit_count) + 1;  // reset to 0 by the schedule kernel
+      int issued = 0;   // K/V ring fills so far
+      int q_loads = 0;  // Q loads so far
       const int my_slice = lane & 7;
-      // Page id and in-page offset of slice my_slice of tile j; out-of-range
-      // slices get page num_blocks, which TMA turns into zero fill.
-      auto lookup = [&](int j, int& pg, int& of) {
-        const int pos = ug.kv_lo + j * kAttnTileN + my_slice * kAttnSlice;
-        const int lp = pos / a.block_size;
-        of = pos - lp * a.block_size;
-        const int lpc = min(lp, a.bt_cols - 1);
-        const int v = load_index(a.block_table, bt_row + lpc, a.bt_i64);
-        pg = (pos < ug.kv_hi && lp < a.bt_cols) ? v : a.num_blocks;
-      };
-      int pg_cur, of_cur, pg_nxt = a.num_blocks, of_nxt = 0;
-      lookup(0, pg_cur, of_cur);
-      if (n_tiles > 1) lookup(1, pg_nxt, of_nxt);
-      int issued = 0;  // ring fills issued so far (fill idx uses slot idx % kKvStages)
-      for (int idx = 0; idx < 2 * n_tiles; ++idx) {
-        const int j = idx >> 1;
-        const bool is_v = idx & 1;
-        const int slot = idx % kKvStages;
-        const uint32_t ph = (idx / kKvStages) & 1;
-        if (!is_v && j > 0) {
-          pg_cur = pg_nxt;
-          of_cur = of_nxt;
-          if (j + 1 < n_tiles) lookup(j + 1, pg_nxt, of_nxt);
+      for (int it = 0;; ++it) {
+        int u = 0;
+        if (lane == 0) u = atomicAdd(claim, 1);
+        u = __shfl_sync(0xffffffffu, u, 0);
+        UnitEntry e{};
+        e.valid = u < unit_count;
+        if (e.valid) {
+          const int4 un = a.units[u];
+          e.seq = un.x;
+          e.qunit = un.y;
+          e.kvh = un.z;
+          e.split = un.w;
+          e.q_begin = load_index(a.cu_q, e.seq, a.len_i64);
+          e.q_end = load_index(a.cu_q, e.seq + 1, a.len_i64);
+          e.seq_len = load_index(a.seqused, e.seq, a.len_i64);
         }
-        const int c = (lane >> 1) & 7;
-        const int page = __shfl_sync(0xffffffffu, pg_cur, c);
-        const int off = __shfl_sync(0xffffffffu, of_cur, c);
         int ok = 1;
         if (lane == 0) {
-          ok = mbar_wait(bar(BAR_KV_EMPTY + slot), ph ^ 1, abort_flag);
-          if (ok) mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), 32768);
+          const int r = it % kUnitRing;
+          ok = mbar_wait(bar(BAR_IT_EMPTY + r), ((it / kUnitRing) & 1) ^ 1, abort_flag);
+          if (ok) {
+            ring[r].seq = e.seq;
+            ring[r].qunit = e.qunit;
+            ring[r].kvh = e.kvh;
+            ring[r].split = e.split;
+            ring[r].q_begin = e.q_begin;
+            ring[r].q_end = e.q_end;
+            ring[r].seq_len = e.seq_len;
+            ring[r].valid = e.valid;
+            mbar_arrive(bar(BAR_IT_FULL + r));  // release: the entry is visible to the waiters
+          }
         }
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;  // also orders the expect_tx before the copies
-        if (lane < 16) {
-          const int half = lane & 1;
-          const void* map = is_v ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
-          tma_load_4d(sbase + kSmKV + slot * 32768 + half * 16384 + c * 2048, map, bar(BAR_KV_FULL + slot), half * 64,
-                      off, kvh, page);
+        if (!__shfl_sync(0xffffffffu, ok, 0) || !e.valid) break;
+        const UnitGeom ug = geometry(e);
+        const int n_tiles = ug.n_tiles;
+        if (n_tiles == 0) continue;
+        const bool two = ug.pos0 + P < ug.q_len;
+        if (lane == 0) {
+          ok = mbar_wait(bar(BAR_Q_EMPTY), (q_loads & 1) ^ 1, abort_flag);
+          if (ok) {
+            const int head0 = e.kvh * a.group;
+            const int t0 = ug.q_begin + ug.pos0;
+            mbar_arrive_expect_tx(bar(BAR_Q_FULL), (two ? 2 : 1) * 32768);
+            tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q_FULL), 0, head0, t0);
+            tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q_FULL), 64, head0, t0);
+            if (two) {
+              tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q_FULL), 0, head0, t0 + P);
+              tma_load_3d(sbase + kSmQ + 49152, &tm_q, bar(BAR_Q_FULL), 64, head0, t0 + P);
+            }
+          }
         }
-        ++issued;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        ++q_loads;
+        const int64_t bt_row = static_cast<int64_t>(e.seq) * a.bt_stride;
+        auto lookup = [&](int j, int& pg, int& of) {
+          const int pos = ug.kv_lo + j * kAttnTileN + my_slice * kAttnSlice;
+          const int lp = pos / a.block_size;
+          of = pos - lp * a.block_size;
+          const int lpc = min(lp, a.bt_cols - 1);
+          const int v = load_index(a.block_table, bt_row + lpc, a.bt_i64);
+          pg = (pos < ug.kv_hi && lp < a.bt_cols) ? v : a.num_blocks;
+        };
+        int pg_cur, of_cur, pg_nxt = a.num_blocks, of_nxt = 0;
+        lookup(0, pg_cur, of_cur);
+        if (n_tiles > 1) lookup(1, pg_nxt, of_nxt);
+        bool stop = false;
+        for (int idx = 0; idx < 2 * n_tiles; ++idx) {
+          const int j = idx >> 1;
+          const bool is_v = idx & 1;
+          const int slot = issued % kKvStages;
+          const uint32_t ph = (issued / kKvStages) & 1;
+          if (!is_v && j > 0) {
+            pg_cur = pg_nxt;
+            of_cur = of_nxt;
+            if (j + 1 < n_tiles) lookup(j + 1, pg_nxt, of_nxt);
+          }
+          const int c = (lane >> 1) & 7;
+          const int page = __shfl_sync(0xffffffffu, pg_cur, c);
+          const int off = __shfl_sync(0xffffffffu, of_cur, c);
+          if (lane == 0) {
+            ok = mbar_wait(bar(BAR_KV_EMPTY + slot), ph ^ 1, abort_flag);
+            if (ok) mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), 32768);
+          }
+          if (!__shfl_sync(0xffffffffu, ok, 0)) {  // also orders the expect_tx before the copies
+            stop = true;
+            break;
+          }
+          if (lane < 16) {
+            const int half = lane & 1;
+            const void* map = is_v ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
+            tma_load_4d(sbase + kSmKV + slot * 32768 + half * 16384 + c * 2048, map, bar(BAR_KV_FULL + slot),
+                        half * 64, off, e.kvh, page);
+          }
+          ++issued;
+        }
+        if (stop) break;
       }
-      // Tail: every issued copy must land, and the UMMA commits that release
-      // the slots must arrive, before this CTA's shared memory is reused.
+      // Tail: every issued copy lands, and the UMMA commits that release the
+      // slots arrive, before the CTA's shared memory is given back.
       if (lane == 0) {
-        mbar_wait_drain(bar(BAR_Q), 0);
+        if (q_loads > 0) mbar_wait_drain(bar(BAR_Q_FULL), (q_loads - 1) & 1);
         for (int s = 0; s < kKvStages && s < issued; ++s) {
           const int last_idx = s + kKvStages * ((issued - 1 - s) / kKvStages);
           const uint32_t last = (last_idx / kKvStages) & 1;
@@ -297,10 +382,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!*abort_flag) mbar_wait_drain(bar(BAR_KV_EMPTY + s), last);
         }
       }
-    } else if (warp == 1 && lane == 0 && n_tiles > 0) {
+    } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_qk = umma_idesc_f16(kBF16, 128, 128, false, false);
       constexpr uint32_t idesc_pv = umma_idesc_f16(kBF16, 128, 128, false, true);
+      int fills = 0, q_uses = 0;
+      int tiles_done[2] = {0, 0};  // tiles already processed by query-tile group t
       auto issue_s = [&](int t, uint32_t kslot_addr) {
         const uint32_t q = sbase + kSmQ + t * 32768;
 #pragma unroll
@@ -311,11 +398,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         tc_commit(bar(BAR_S_FULL + t));
       };
-      // O_t += P_t V, a quarter (32 keys, two K16 steps) at a time as the
-      // softmax warpgroup publishes each quarter of P.
-      auto issue_pv = [&](int t, int j, uint32_t vslot_addr, bool acc) {
+      auto issue_pv = [&](int t, int c, uint32_t vslot_addr, bool acc) {
         for (int q = 0; q < 4; ++q) {
-          if (!mbar_wait(bar(BAR_P_FULL + 4 * t + q), j & 1, abort_flag)) return false;
+          if (!mbar_wait(bar(BAR_P_FULL + 4 * t + q), c & 1, abort_flag)) return false;
           tc_fence_after();
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -327,33 +412,58 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_commit(bar(BAR_O_DONE + t));
         return true;
       };
-      auto slot_addr = [&](int idx) { return sbase + kSmKV + (idx % kKvStages) * 32768; };
-      auto wait_full = [&](int idx) {
-        return mbar_wait(bar(BAR_KV_FULL + idx % kKvStages), (idx / kKvStages) & 1, abort_flag);
+      auto slot_addr = [&](int g) { return sbase + kSmKV + (g % kKvStages) * 32768; };
+      auto wait_full = [&](int g) {
+        return mbar_wait(bar(BAR_KV_FULL + g % kKvStages), (g / kKvStages) & 1, abort_flag);
       };
-
-      bool ok = mbar_wait(bar(BAR_Q), 0, abort_flag) && wait_full(0);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, slot_addr(0));
-        if (two) issue_s(1, slot_addr(0));
-        tc_commit(bar(BAR_KV_EMPTY + 0));
-      }
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int vidx = 2 * j + 1, kidx = 2 * j + 2;
-        const bool more = j + 1 < n_tiles;
-        if (!wait_full(vidx) || !issue_pv(0, j, slot_addr(vidx), j > 0)) break;
-        if (more) {
-          if (!wait_full(kidx)) break;
+      for (int it = 0;; ++it) {
+        UnitEntry e;
+        if (!take_entry(it, e)) break;
+        mbar_arrive(bar(BAR_IT_EMPTY + it % kUnitRing));
+        if (!e.valid) break;
+        const UnitGeom ug = geometry(e);
+        const int n_tiles = ug.n_tiles;
+        if (n_tiles == 0) continue;
+        const bool two = ug.pos0 + P < ug.q_len;
+        bool ok = mbar_wait(bar(BAR_Q_FULL), q_uses & 1, abort_flag) && wait_full(fills);
+        if (ok) {
           tc_fence_after();
-          issue_s(0, slot_addr(kidx));
+          issue_s(0, slot_addr(fills));
+          if (two) issue_s(1, slot_addr(fills));
+          if (n_tiles == 1) tc_commit(bar(BAR_Q_EMPTY));
+          tc_commit(bar(BAR_KV_EMPTY + fills % kKvStages));
         }
-        if (two) {
-          if (!issue_pv(1, j, slot_addr(vidx), j > 0)) break;
-          if (more) issue_s(1, slot_addr(kidx));
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int vidx = fills + 2 * j + 1, kidx = fills + 2 * j + 2;
+          const bool more = j + 1 < n_tiles;
+          if (!wait_full(vidx) || !issue_pv(0, tiles_done[0] + j, slot_addr(vidx), j > 0)) {
+            ok = false;
+            break;
+          }
+          if (more) {
+            if (!wait_full(kidx)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(0, slot_addr(kidx));
+          }
+          if (two) {
+            if (!issue_pv(1, tiles_done[1] + j, slot_addr(vidx), j > 0)) {
+              ok = false;
+              break;
+            }
+            if (more) issue_s(1, slot_addr(kidx));
+          }
+          if (more && j + 2 == n_tiles) tc_commit(bar(BAR_Q_EMPTY));  // the unit's last S is issued
+          tc_commit(bar(BAR_KV_EMPTY + vidx % kKvStages));
+          if (more) tc_commit(bar(BAR_KV_EMPTY + kidx % kKvStages));
         }
-        tc_commit(bar(BAR_KV_EMPTY + vidx % kKvStages));
-        if (more) tc_commit(bar(BAR_KV_EMPTY + kidx % kKvStages));
+        if (!ok) break;
+        fills += 2 * n_tiles;
+        ++q_uses;
+        tiles_done[0] += n_tiles;
+        if (two) tiles_done[1] += n_tiles;
       }
       // All MMAs issued so far complete before the CTA may free TMEM.
       tc_commit(bar(BAR_DRAIN));
@@ -363,20 +473,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kAttnSoftmaxRegs));
     // ------------------------------------------------------------ softmax (tile t)
     const int t = (warp - 4) >> 2;
-    if (t == 0 || two) {
-      const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
-      const int row = quarter * 32 + lane;
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + t * 128;
+    const uint32_t o_addr = tmem + lane_base + 256 + t * 128;
+    const float sl2 = a.scale_log2;
+    int fills = 0;       // K/V ring fills of the units before this one
+    int tiles_done = 0;  // tiles this group processed in earlier units
+    bool aborted = false;
+    for (int it = 0; !aborted; ++it) {
+      UnitEntry e;
+      if (!take_entry(it, e)) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(BAR_IT_EMPTY + it % kUnitRing));
+      if (!e.valid) break;
+      const UnitGeom ug = geometry(e);
+      const int n_tiles = ug.n_tiles;
+      const bool two = ug.pos0 + P < ug.q_len;
+      const int unit_fills = fills;
+      fills += 2 * n_tiles;
+      if (!(t == 0 || two)) continue;
       const int tile_pos0 = ug.pos0 + t * P;
       const int row_pos = tile_pos0 + row / a.group;
-      const int row_head = kvh * a.group + row % a.group;
+      const int row_head = e.kvh * a.group + row % a.group;
       const bool row_valid = row_pos < ug.q_len;
       const int q_abs = ug.q_abs_min + t * P + row / a.group;
       const int row_hi = min(ug.split_end, q_abs + 1);
       const int unmasked_hi = min(ug.split_end, ug.q_abs_min + t * P + 1);
-      const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-      const uint32_t s_addr = tmem + lane_base + t * 128;
-      const uint32_t o_addr = tmem + lane_base + 256 + t * 128;
-      const float sl2 = a.scale_log2;
       // V rows [v_tail_from, v_tail_to) of the last tile: loaded page rows at or past L.
       const int last_start = ug.kv_lo + (n_tiles - 1) * kAttnTileN;
       const int v_tail_from = max(ug.seq_len - last_start, 0);
@@ -384,9 +508,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
       float m_used = -INFINITY;  // running maximum in scaled base-2 units
       float l = 0.f;
-      bool aborted = false;
       for (int j = 0; j < n_tiles; ++j) {
-        if (!mbar_wait(bar(BAR_S_FULL + t), j & 1, abort_flag)) {
+        const int c = tiles_done + j;
+        if (!mbar_wait(bar(BAR_S_FULL + t), c & 1, abort_flag)) {
           aborted = true;
           break;
         }
@@ -405,12 +529,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4)
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const int col = c4 * 32 + c;
-              if (col < lo || col >= hi) sr[c4][c] = __float_as_uint(-INFINITY);
+            for (int cc = 0; cc < 32; ++cc) {
+              const int col = c4 * 32 + cc;
+              if (col < lo || col >= hi) sr[c4][cc] = __float_as_uint(-INFINITY);
             }
         }
-        // Row maximum: eight independent chains of three-input max.
         float mx[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
@@ -428,7 +551,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const float alpha = raise ? ex2_approx(m_used - m_cand) : 1.f;  // 0 when m_used = -inf
           if (j > 0) {
             // O holds PV of tiles < j: scale it before PV_j accumulates.
-            if (!mbar_wait(bar(BAR_O_DONE + t), (j - 1) & 1, abort_flag)) {
+            if (!mbar_wait(bar(BAR_O_DONE + t), (c - 1) & 1, abort_flag)) {
               aborted = true;
               break;
             }
@@ -439,7 +562,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               tmem_ld16(o_addr + 16 * c8, o);
               tmem_wait_ld16(o);
 #pragma unroll
-              for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+              for (int cc = 0; cc < 16; ++cc) o[cc] = __float_as_uint(__uint_as_float(o[cc]) * alpha);
               tmem_st16(o_addr + 16 * c8, o);
             }
           }
@@ -453,8 +576,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           // Rows of the last page past the sequence end may hold anything (NaN
           // included); P is 0 there but 0 * NaN is NaN, so zero those V rows,
           // as the reference's masked V load does (triton_split_kv_paged.py:122).
-          // Done before the first quarter of P is published.
-          const int vidx = 2 * j + 1;
+          const int vidx = unit_fills + 2 * j + 1;
           if (!mbar_wait(bar(BAR_KV_FULL + vidx % kKvStages), (vidx / kKvStages) & 1, abort_flag)) {
             aborted = true;
             break;
@@ -469,11 +591,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           fence_proxy_async_smem();
         }
 
-        // P over the first 64 columns of S_t (column c = keys 2c, 2c+1), stored
-        // and published a quarter (32 keys) at a time so that the PV UMMAs of
-        // this tile run while the rest of P is computed; S is already in
-        // registers.  Scale-and-subtract and the row sum run as f32x2 pairs
-        // (half the issue slots); exp2 on the special-function unit.
         const uint64_t sl2_2 = f2_pack(sl2, sl2), negm_2 = f2_pack(neg_m, neg_m);
         uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
 #pragma unroll
@@ -503,44 +620,44 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
       // ---------------------------------------------------------- epilogue
       if (!aborted && n_tiles > 0) {
-        if (!mbar_wait(bar(BAR_O_DONE + t), (n_tiles - 1) & 1, abort_flag)) aborted = true;
+        if (!mbar_wait(bar(BAR_O_DONE + t), (tiles_done + n_tiles - 1) & 1, abort_flag)) aborted = true;
         tc_fence_after();
       }
-      if (!aborted) {
-        const float inv = 1.f / fmaxf(l, 1e-20f);
-        const int tok = ug.q_begin + row_pos;
-        T* dst;
-        if (a.num_splits == 1) {
-          dst = static_cast<T*>(a.out) + static_cast<int64_t>(tok) * a.out_st + static_cast<int64_t>(row_head) * a.out_sh;
-        } else {
-          const int64_t rowi = (static_cast<int64_t>(split) * a.total_q + tok) * a.num_q_heads + row_head;
-          dst = static_cast<T*>(a.o_split) + rowi * kAttnHeadDim;
-          if (row_valid) {
-            a.m_split[rowi] = (l > 0.f) ? m_used * 0.69314718055994530942f : -INFINITY;
-            a.l_split[rowi] = l;
-          }
+      tiles_done += n_tiles;
+      if (aborted) break;
+      const float inv = 1.f / fmaxf(l, 1e-20f);
+      const int tok = ug.q_begin + row_pos;
+      T* dst;
+      if (a.num_splits == 1) {
+        dst = static_cast<T*>(a.out) + static_cast<int64_t>(tok) * a.out_st + static_cast<int64_t>(row_head) * a.out_sh;
+      } else {
+        const int64_t rowi = (static_cast<int64_t>(e.split) * a.total_q + tok) * a.num_q_heads + row_head;
+        dst = static_cast<T*>(a.o_split) + rowi * kAttnHeadDim;
+        if (row_valid) {
+          a.m_split[rowi] = (l > 0.f) ? m_used * 0.69314718055994530942f : -INFINITY;
+          a.l_split[rowi] = l;
         }
+      }
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t o[32];
-          if (n_tiles > 0) {
-            tmem_ld32(o_addr + 32 * c4, o);
-            tmem_wait_ld(o);
-          } else {
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        if (n_tiles > 0) {
+          tmem_ld32(o_addr + 32 * c4, o);
+          tmem_wait_ld(o);
+        } else {
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = 0u;
-          }
-          if (row_valid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
+          for (int cc = 0; cc < 32; ++cc) o[cc] = 0u;
+        }
+        if (row_valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = Pack2<T>::pack(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-              w.y = Pack2<T>::pack(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-              w.z = Pack2<T>::pack(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-              w.w = Pack2<T>::pack(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-              d4[v] = w;
-            }
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = Pack2<T>::pack(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+            w.y = Pack2<T>::pack(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+            w.z = Pack2<T>::pack(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+            w.w = Pack2<T>::pack(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+            d4[v] = w;
           }
         }
       }
@@ -559,9 +676,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Device-side work list: one block, bucket sort of units by KV-tile count,
-// heaviest first, so the hardware's in-order CTA dispatch approximates a
-// longest-processing-time schedule.  No host synchronisation is needed: the
-// attention grid is sized to an upper bound and surplus CTAs exit at once.
+// heaviest first; the persistent attention CTAs claim units in this order
+// (a longest-processing-time schedule).  No host synchronisation is needed:
+// the unit count and the claim counter stay on the device.
 // ---------------------------------------------------------------------------
 constexpr int kSchedThreads = 1024;
 constexpr int kSchedBuckets = 2048;
@@ -687,7 +804,10 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
     const int slot = atomicAdd(&hist[bucket], 1);
     a.units[slot] = make_int4(seq, qtile, kvh, split);
   }
-  if (threadIdx.x == 0) *a.unit_count = total_units;
+  if (threadIdx.x == 0) {
+    a.unit_count[0] = total_units;
+    a.unit_count[1] = 0;  // claim counter of the persistent attention kernel
+  }
 }
 
 }  // namespace b200

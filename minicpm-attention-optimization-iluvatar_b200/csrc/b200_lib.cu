@@ -84,7 +84,7 @@ int encode_map(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank, const 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct WorkspaceLayout {
-  size_t count_off, tile_base_off, units_off, o_off, m_off, l_off, total;
+  size_t count_off, tile_base_off, seq_off_off, units_off, o_off, m_off, l_off, total;
   int capacity;
 };
 
@@ -98,7 +98,8 @@ WorkspaceLayout attn_workspace_layout(int64_t total_q, int num_seqs, int hq, int
   w.capacity = static_cast<int>(cap > 0x7fffffff ? 0x7fffffff : cap);
   w.count_off = 0;
   w.tile_base_off = 256;
-  w.units_off = align_up(w.tile_base_off + sizeof(int) * (num_seqs + 1), 256);
+  w.seq_off_off = align_up(w.tile_base_off + sizeof(int) * (num_seqs + 1), 256);
+  w.units_off = align_up(w.seq_off_off + sizeof(int) * num_seqs, 256);
   w.o_off = align_up(w.units_off + sizeof(int4) * static_cast<size_t>(w.capacity), 256);
   w.m_off = w.o_off;
   w.l_off = w.o_off;
@@ -172,6 +173,26 @@ int auto_splits(int32_t total_q, int32_t num_seqs, int32_t hq, int32_t hkv, int3
 }
 
 // Decode batch: schedule (items per sequence), persistent decode kernel, combine.
+// Per KV head: (d, key % 8, half of head_dim, key / 8 in the page, page); one
+// box = a 16-key page slice with both halves (4 KB).  Needs num_kv_heads <=
+// kMaxHeadMaps and block_size % 16 == 0.
+int encode_kv_head_maps(const B200AttnParams* p, CUtensorMapDataType dt, b200::KvHeadMaps* maps) {
+  const int elt = 2;
+  memset(maps, 0, sizeof(*maps));
+  for (int h = 0; h < p->num_kv_heads; ++h) {
+    for (int kv = 0; kv < 2; ++kv) {
+      const uint8_t* base = static_cast<const uint8_t*>(kv ? p->v : p->k) +
+                            (int64_t)h * (kv ? p->v_stride_head : p->k_stride_head) * elt;
+      const int64_t st = kv ? p->v_stride_tok : p->k_stride_tok, sb = kv ? p->v_stride_block : p->k_stride_block;
+      const cuuint64_t dims[5] = {64, 8, 2, (cuuint64_t)(p->block_size / 8), (cuuint64_t)p->num_blocks};
+      const cuuint64_t strides[4] = {(cuuint64_t)(st * elt), 128, (cuuint64_t)(8 * st * elt), (cuuint64_t)(sb * elt)};
+      const cuuint32_t box[5] = {64, 8, 2, 2, 1};
+      if (int r = encode_map(kv ? &maps->v[h] : &maps->k[h], dt, 5, base, dims, strides, box, kv ? "v" : "k")) return r;
+    }
+  }
+  return B200_OK;
+}
+
 int run_decode(const B200AttnParams* p, cudaStream_t s, int group) {
   const int elt = 2;
   const int sms = sm_count();
@@ -189,21 +210,8 @@ int run_decode(const B200AttnParams* p, cudaStream_t s, int group) {
     const cuuint32_t box[3] = {64, (cuuint32_t)group, 1};
     if (int r = encode_map(&tm_q, dt, 3, p->q, dims, strides, box, "q")) return r;
   }
-  // Per KV head: (d, key % 8, half of head_dim, key / 8 in the page, page); one
-  // box = a 16-key page slice with both halves (4 KB).
   b200::DecodeMaps maps;
-  memset(&maps, 0, sizeof(maps));
-  for (int h = 0; h < p->num_kv_heads; ++h) {
-    for (int kv = 0; kv < 2; ++kv) {
-      const uint8_t* base = static_cast<const uint8_t*>(kv ? p->v : p->k) +
-                            (int64_t)h * (kv ? p->v_stride_head : p->k_stride_head) * elt;
-      const int64_t st = kv ? p->v_stride_tok : p->k_stride_tok, sb = kv ? p->v_stride_block : p->k_stride_block;
-      const cuuint64_t dims[5] = {64, 8, 2, (cuuint64_t)(p->block_size / 8), (cuuint64_t)p->num_blocks};
-      const cuuint64_t strides[4] = {(cuuint64_t)(st * elt), 128, (cuuint64_t)(8 * st * elt), (cuuint64_t)(sb * elt)};
-      const cuuint32_t box[5] = {64, 8, 2, 2, 1};
-      if (int r = encode_map(kv ? &maps.v[h] : &maps.k[h], dt, 5, base, dims, strides, box, kv ? "v" : "k")) return r;
-    }
-  }
+  if (int r = encode_kv_head_maps(p, dt, &maps)) return r;
   b200::DecodeArgs a{};
   a.block_table = p->block_table;
   a.cu_q = p->cu_seqlens_q;
@@ -415,8 +423,18 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   }
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // CTA-pair kernel (M = 256 UMMA across two SMs) or single-CTA kernel.
+  // CTA-pair kernel (M = 256 UMMA across two SMs) or single-CTA kernel; the
+  // single-CTA kernel takes per-KV-head maps (4 KB boxes) when they fit.
   const bool pair = use_cta_pair();
+  const bool head_maps = !pair && p->num_kv_heads <= b200::kMaxHeadMaps;
+  b200::KvHeadMaps maps;
+  if (head_maps) {
+    if (int r = encode_kv_head_maps(p, dt, &maps)) return r;
+  } else {
+    memset(&maps, 0, sizeof(maps));
+    maps.k[0] = tm_k;
+    maps.v[0] = tm_v;
+  }
   const int units_per_tile_group = pair ? b200::kPairTilesPerUnit : b200::kAttnTilesPerUnit;
   b200::SchedArgs sa{};
   sa.cu_q = p->cu_seqlens_q;
@@ -428,6 +446,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   sa.num_splits = splits;
   sa.capacity = w.capacity;
   sa.tile_base = reinterpret_cast<int*>(ws + w.tile_base_off);
+  sa.seq_off = reinterpret_cast<int*>(ws + w.seq_off_off);
   sa.units = reinterpret_cast<int4*>(ws + w.units_off);
   sa.unit_count = reinterpret_cast<int*>(ws + w.count_off);
   b200::attn_schedule_kernel<<<1, b200::kSchedThreads, 0, s>>>(sa);
@@ -465,7 +484,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   const int64_t ctas = units_ub * p->num_kv_heads * splits * (pair ? 2 : 1);
   // The single-CTA kernel is persistent: one CTA per SM at most.
   const dim3 grid(static_cast<unsigned>(pair ? ctas : std::min<int64_t>(ctas, sm_count())));
-  auto launch = [&](auto kernel) -> int {
+  auto launch = [&](auto kernel, const auto&... args) -> int {
     // The kernel rebalances registers between warpgroups with setmaxnreg; the
     // split adds up only if every thread was launched with exactly
     // kAttnLaunchRegs registers, so refuse to launch otherwise.
@@ -487,16 +506,20 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
     cfg.stream = s;
     cfg.attrs = pdl;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, kernel, tm_q, tm_k, tm_v, a);
+    cudaLaunchKernelEx(&cfg, kernel, args...);
     return B200_OK;
   };
+  const bool bf16 = p->dtype == B200_DTYPE_BF16;
   int lr;
   if (pair)
-    lr = (p->dtype == B200_DTYPE_BF16) ? launch(b200::paged_attn_fwd_pair_kernel<__nv_bfloat16>)
-                                       : launch(b200::paged_attn_fwd_pair_kernel<__half>);
+    lr = bf16 ? launch(b200::paged_attn_fwd_pair_kernel<__nv_bfloat16>, tm_q, tm_k, tm_v, a)
+              : launch(b200::paged_attn_fwd_pair_kernel<__half>, tm_q, tm_k, tm_v, a);
+  else if (head_maps)
+    lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, true>, tm_q, maps, a)
+              : launch(b200::paged_attn_fwd_kernel<__half, true>, tm_q, maps, a);
   else
-    lr = (p->dtype == B200_DTYPE_BF16) ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16>)
-                                       : launch(b200::paged_attn_fwd_kernel<__half>);
+    lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, false>, tm_q, maps, a)
+              : launch(b200::paged_attn_fwd_kernel<__half, false>, tm_q, maps, a);
   if (lr != B200_OK) return lr;
   if (int r = check_launch("paged_attn_fwd_kernel")) return r;
 

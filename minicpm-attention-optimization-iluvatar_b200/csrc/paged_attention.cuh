@@ -130,6 +130,26 @@ struct AttnKernelArgs {
   float scale_log2;   // softmax_scale * log2(e)
 };
 
+// K/V tensor maps.  Up to kMaxHeadMaps KV heads: one 5-D map per head,
+// (d % 64, key % 8, half of head_dim, key / 8 in the page, page), whose box is
+// a 16-key page slice with both halves (4 KB): 8 boxes per 128-key tile.  More
+// heads: k[0] / v[0] hold a 4-D map (d, key in the page, head, page) whose box
+// is one half of a slice (2 KB): 16 boxes per tile.  The TMA unit's per-box
+// cost makes the box count matter (2 KB boxes instead of 4 KB cost 10 % at 16K).
+constexpr int kMaxHeadMaps = 8;
+struct KvHeadMaps {
+  CUtensorMap k[kMaxHeadMaps];
+  CUtensorMap v[kMaxHeadMaps];
+};
+
+// Shared-memory offset of the 16-byte piece `chunk` of row r (a key) of half h
+// in one K/V ring slot.  Per-head maps: 8-key groups of 2 KB, each holding both
+// halves (8 rows of 128 B each); 4-D maps: two 16 KB halves of 128 rows.
+template <bool kHeadMaps>
+__device__ __forceinline__ uint32_t kv_slot_offset(int r, int h, int chunk) {
+  return kHeadMaps ? (r >> 3) * 2048 + h * 1024 + (r & 7) * 128 + chunk * 16 : h * 16384 + r * 128 + chunk * 16;
+}
+
 __device__ __forceinline__ int load_index(const void* p, int64_t i, int is_i64) {
   return is_i64 ? static_cast<int>(static_cast<const int64_t*>(p)[i]) : static_cast<const int*>(p)[i];
 }
@@ -192,10 +212,10 @@ __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
   }
 }
 
-template <typename T>
+template <typename T, bool kHeadMaps>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    paged_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const AttnKernelArgs a) {
+    paged_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ KvHeadMaps maps,
+                          const AttnKernelArgs a) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   griddep_wait();  // launched as a programmatic dependent of the schedule kernel
 
@@ -264,10 +284,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kAttnProducerRegs));
     if (warp == 0) {
       // ---------------------------------------------------------- producer (whole warp)
-      if (lane == 0) {
-        tma_prefetch_desc(&tm_q);
-        tma_prefetch_desc(&tm_k);
-        tma_prefetch_desc(&tm_v);
+      if (lane == 0) tma_prefetch_desc(&tm_q);
+      if (lane < (kHeadMaps ? a.num_q_heads / a.group : 1)) {
+        tma_prefetch_desc(&maps.k[lane]);
+        tma_prefetch_desc(&maps.v[lane]);
       }
       const int unit_count = *a.unit_count;
       int* claim = const_cast<int*>(a.unit_count) + 1;  // reset to 0 by the schedule kernel
@@ -350,9 +370,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             of_cur = of_nxt;
             if (j + 1 < n_tiles) lookup(j + 1, pg_nxt, of_nxt);
           }
+          // 4-D maps: lanes 0..15 issue half c = lane & 1 of slice (lane >> 1).
           const int c = (lane >> 1) & 7;
-          const int page = __shfl_sync(0xffffffffu, pg_cur, c);
-          const int off = __shfl_sync(0xffffffffu, of_cur, c);
+          const int page = kHeadMaps ? pg_cur : __shfl_sync(0xffffffffu, pg_cur, c);
+          const int off = kHeadMaps ? of_cur : __shfl_sync(0xffffffffu, of_cur, c);
           if (lane == 0) {
             ok = mbar_wait(bar(BAR_KV_EMPTY + slot), ph ^ 1, abort_flag);
             if (ok) mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), 32768);
@@ -361,9 +382,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             stop = true;
             break;
           }
-          if (lane < 16) {
+          if (kHeadMaps) {
+            // lane c < 8 issues slice c (its own lookup): 16 keys x both halves.
+            if (lane < 8) {
+              const CUtensorMap* map = is_v ? &maps.v[e.kvh] : &maps.k[e.kvh];
+              tma_load_5d(sbase + kSmKV + slot * 32768 + lane * 4096, map, bar(BAR_KV_FULL + slot), 0, 0, 0,
+                          off >> 3, page);
+            }
+          } else if (lane < 16) {
             const int half = lane & 1;
-            const void* map = is_v ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
+            const CUtensorMap* map = is_v ? &maps.v[0] : &maps.k[0];
             tma_load_4d(sbase + kSmKV + slot * 32768 + half * 16384 + c * 2048, map, bar(BAR_KV_FULL + slot),
                         half * 64, off, e.kvh, page);
           }
@@ -392,9 +420,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t q = sbase + kSmQ + t * 32768;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_ss(tmem + t * 128, umma_desc_sw128(q + koff, 16, 1024), umma_desc_sw128(kslot_addr + koff, 16, 1024),
-                  idesc_qk, kk > 0);
+          const uint32_t qoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t koff = kv_slot_offset<kHeadMaps>(0, kk >> 2, 0) + (kk & 3) * 32;
+          umma_ss(tmem + t * 128, umma_desc_sw128(q + qoff, 16, 1024),
+                  umma_desc_sw128(kslot_addr + koff, 16, kHeadMaps ? 2048 : 1024), idesc_qk, kk > 0);
         }
         tc_commit(bar(BAR_S_FULL + t));
       };
@@ -405,7 +434,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int kk = 2 * q + h;
-            umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, umma_desc_sw128(vslot_addr + kk * 2048, 16384, 1024),
+            // V is the MN-major B operand: 64-column atoms at LBO, 8-key groups at SBO.
+            umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                    umma_desc_sw128(vslot_addr + kv_slot_offset<kHeadMaps>(16 * kk, 0, 0), kHeadMaps ? 1024 : 16384,
+                                    kHeadMaps ? 2048 : 1024),
                     idesc_pv, (acc || kk > 0) ? 1u : 0u);
           }
         }
@@ -586,7 +618,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = threadIdx.x - 128; i < n16; i += 128) {
             const int r = v_tail_from + (i >> 4);
             const int half = (i >> 3) & 1;
-            st_shared_v4(vbase + half * 16384 + r * 128 + (i & 7) * 16, 0u, 0u, 0u, 0u);
+            st_shared_v4(vbase + kv_slot_offset<kHeadMaps>(r, half, i & 7), 0u, 0u, 0u, 0u);
           }
           fence_proxy_async_smem();
         }
@@ -675,13 +707,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 
 // ---------------------------------------------------------------------------
-// Device-side work list: one block, bucket sort of units by KV-tile count,
-// heaviest first; the persistent attention CTAs claim units in this order
-// (a longest-processing-time schedule).  No host synchronisation is needed:
-// the unit count and the claim counter stay on the device.
+// Device-side work list, built by one block with no host synchronisation.
+// Order: sequences by estimated work, heaviest first (a bucket sort on a log
+// scale); inside a sequence, query units from the last (most keys) to the
+// first, the KV heads and splits of one query unit side by side.  The
+// persistent attention CTAs claim units in this order, which is a
+// longest-processing-time schedule at sequence granularity (the last
+// kSchedThreads units are re-sorted by size across sequences) and keeps the
+// CTAs running at any moment on a few sequences, so each sequence's K/V pages
+// are read from HBM about once and then served from L2 (ordering units by
+// size alone interleaved all sequences and read the 16K workload's K/V from
+// HBM six times over).  The unit count and the claim counter stay on the
+// device.
 // ---------------------------------------------------------------------------
 constexpr int kSchedThreads = 1024;
 constexpr int kSchedBuckets = 2048;
+constexpr float kSchedBucketsPerOctave = 46.0f;  // 2^44 (the largest work estimate) -> bucket 2024
 
 struct SchedArgs {
   const void* cu_q;
@@ -692,9 +733,10 @@ struct SchedArgs {
   int num_kv_heads;
   int num_splits;
   int capacity;
-  int* tile_base;  // [num_seqs + 1]
+  int* tile_base;  // [num_seqs + 1]: query units per sequence, exclusive prefix
+  int* seq_off;    // [num_seqs]: first slot of each sequence's units in the work list
   int4* units;
-  int* unit_count;
+  int* unit_count;  // [0] units, [1] claim counter of the attention kernel
 };
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& total) {
@@ -723,13 +765,43 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& 
   return before;
 }
 
+// hist[i] := number of entries in buckets above i (exclusive prefix from the
+// top bucket down).
+__device__ __forceinline__ void buckets_to_offsets_desc(int* hist, int* warp_sums) {
+  constexpr int per = kSchedBuckets / kSchedThreads;
+  int local[per];
+  int sum = 0;
+#pragma unroll
+  for (int k = 0; k < per; ++k) {
+    local[k] = hist[kSchedBuckets - 1 - (threadIdx.x * per + k)];
+    sum += local[k];
+  }
+  int total;
+  int before = block_exclusive_scan(sum, warp_sums, total);
+#pragma unroll
+  for (int k = 0; k < per; ++k) {
+    hist[kSchedBuckets - 1 - (threadIdx.x * per + k)] = before;
+    before += local[k];
+  }
+}
+
+// Sort bucket of sequence b: log2 of (query units x mean causal key count),
+// the sequence's share of the work up to a constant.
+__device__ __forceinline__ int seq_bucket(const SchedArgs& a, int b, int units) {
+  const int ql = load_index(a.cu_q, b + 1, a.len_i64) - load_index(a.cu_q, b, a.len_i64);
+  const int L = load_index(a.seqused, b, a.len_i64);
+  const float keys = fmaxf(static_cast<float>(L) - 0.5f * static_cast<float>(ql), 1.0f);
+  const float work = static_cast<float>(units) * keys;
+  return min(kSchedBuckets - 1, max(0, static_cast<int>(__log2f(work) * kSchedBucketsPerOctave)));
+}
+
 __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const SchedArgs a) {
   __shared__ int hist[kSchedBuckets];
   __shared__ int warp_sums[32];
   __shared__ int s_total_tiles;
   griddep_launch_dependents();  // the attention grid may launch; it waits for this one
 
-  // 1. query tiles per sequence, exclusive prefix over sequences.
+  // 1. query units per sequence, exclusive prefix over sequences.
   int carry = 0;
   for (int base = 0; base < a.num_seqs; base += kSchedThreads) {
     const int b = base + threadIdx.x;
@@ -753,57 +825,62 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   const int per_tile = a.num_kv_heads * a.num_splits;
   const int total_units = min(s_total_tiles * per_tile, a.capacity);
 
-  auto decode = [&](int u, int& seq, int& qtile, int& kvh, int& split, int& bucket) {
+  // 2. units per work bucket.
+  for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
+    const int qt = a.tile_base[b + 1] - a.tile_base[b];
+    if (qt > 0) atomicAdd(&hist[seq_bucket(a, b, qt)], qt * per_tile);
+  }
+  __syncthreads();
+  // 3. bucket offsets, heaviest bucket first.
+  buckets_to_offsets_desc(hist, warp_sums);
+  __syncthreads();
+  // 4. each sequence takes a contiguous range of its bucket.
+  for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
+    const int qt = a.tile_base[b + 1] - a.tile_base[b];
+    if (qt > 0) a.seq_off[b] = atomicAdd(&hist[seq_bucket(a, b, qt)], qt * per_tile);
+  }
+  __syncthreads();
+  // 5. scatter: unit u = (query tile, KV head, split) in natural order goes to
+  // its sequence's range, last query unit first.
+  for (int u = threadIdx.x; u < total_units; u += kSchedThreads) {
     const int tile = u / per_tile;
     const int rem = u - tile * per_tile;
-    kvh = rem / a.num_splits;
-    split = rem - kvh * a.num_splits;
+    const int kvh = rem / a.num_splits;
+    const int split = rem - kvh * a.num_splits;
     int lo = 0, hi = a.num_seqs - 1;  // last seq with tile_base[seq] <= tile
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (a.tile_base[mid] <= tile) lo = mid; else hi = mid - 1;
     }
-    seq = lo;
-    qtile = tile - a.tile_base[seq];
-    const UnitGeom g = unit_geometry(load_index(a.cu_q, seq, a.len_i64), load_index(a.cu_q, seq + 1, a.len_i64),
-                                     load_index(a.seqused, seq, a.len_i64), qtile, split, a.pos_per_unit,
+    const int seq = lo;
+    const int qtile = tile - a.tile_base[seq];
+    const int qt = a.tile_base[seq + 1] - a.tile_base[seq];
+    const int slot = a.seq_off[seq] + (qt - 1 - qtile) * per_tile + rem;
+    if (slot < a.capacity) a.units[slot] = make_int4(seq, qtile, kvh, split);
+  }
+  __syncthreads();
+  // 6. the schedule's tail, its last kSchedThreads units, by KV-tile count
+  // across sequences, heaviest first, so the last units claimed are the
+  // smallest.
+  const int tail = min(total_units, kSchedThreads);
+  const int tail0 = total_units - tail;
+  const bool mine = static_cast<int>(threadIdx.x) < tail;
+  int4 unit = make_int4(0, 0, 0, 0);
+  int bucket = 0;
+  if (mine) {
+    unit = a.units[tail0 + threadIdx.x];
+    const UnitGeom g = unit_geometry(load_index(a.cu_q, unit.x, a.len_i64), load_index(a.cu_q, unit.x + 1, a.len_i64),
+                                     load_index(a.seqused, unit.x, a.len_i64), unit.y, unit.w, a.pos_per_unit,
                                      a.num_splits);
     bucket = min(g.n_tiles, kSchedBuckets - 1);
-  };
-
-  // 2. histogram of KV-tile counts.
-  for (int u = threadIdx.x; u < total_units; u += kSchedThreads) {
-    int seq, qtile, kvh, split, bucket;
-    decode(u, seq, qtile, kvh, split, bucket);
-    atomicAdd(&hist[bucket], 1);
   }
+  for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;
   __syncthreads();
-  // 3. bucket offsets, heaviest bucket first.
-  {
-    constexpr int per = kSchedBuckets / kSchedThreads;
-    int local[per];
-    int sum = 0;
-#pragma unroll
-    for (int k = 0; k < per; ++k) {
-      local[k] = hist[kSchedBuckets - 1 - (threadIdx.x * per + k)];
-      sum += local[k];
-    }
-    int total;
-    int before = block_exclusive_scan(sum, warp_sums, total);
-#pragma unroll
-    for (int k = 0; k < per; ++k) {
-      hist[kSchedBuckets - 1 - (threadIdx.x * per + k)] = before;
-      before += local[k];
-    }
-  }
+  if (mine) atomicAdd(&hist[bucket], 1);
   __syncthreads();
-  // 4. scatter.
-  for (int u = threadIdx.x; u < total_units; u += kSchedThreads) {
-    int seq, qtile, kvh, split, bucket;
-    decode(u, seq, qtile, kvh, split, bucket);
-    const int slot = atomicAdd(&hist[bucket], 1);
-    a.units[slot] = make_int4(seq, qtile, kvh, split);
-  }
+  buckets_to_offsets_desc(hist, warp_sums);
+  __syncthreads();
+  if (mine) a.units[tail0 + atomicAdd(&hist[bucket], 1)] = unit;
   if (threadIdx.x == 0) {
     a.unit_count[0] = total_units;
     a.unit_count[1] = 0;  // claim counter of the persistent attention kernel

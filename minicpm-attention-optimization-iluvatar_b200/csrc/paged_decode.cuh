@@ -45,7 +45,7 @@ constexpr int kDecThreads = 256;
 constexpr int kDecTileN = 128;     // keys per tile (UMMA M of S^T)
 constexpr int kDecN = 16;          // UMMA N: query heads of a group, zero-padded
 constexpr int kDecStages = 3;      // slots of 32 KB in each of the K and V rings
-constexpr int kDecMaxKvHeads = 8;  // per-head tensor maps passed as kernel parameters
+constexpr int kDecMaxKvHeads = kMaxHeadMaps;  // per-head tensor maps passed as kernel parameters
 constexpr int kDecTmemCols = 64;   // S^T ring 2 x 16 columns, O^T 2 x 16 columns
 constexpr float kDecRescale = 8.0f;
 
@@ -98,10 +98,7 @@ struct DecodeArgs {
 };
 
 // One 5-D tensor map per KV head for each of K and V (see the header comment).
-struct DecodeMaps {
-  CUtensorMap k[kDecMaxKvHeads];
-  CUtensorMap v[kDecMaxKvHeads];
-};
+using DecodeMaps = KvHeadMaps;
 
 struct DecodeItem {
   int seq, kvh, kv_begin, kv_end, L, n_tiles;
@@ -171,23 +168,7 @@ __global__ void __launch_bounds__(kSchedThreads, 1) decode_schedule_kernel(const
   auto bucket_of = [&](int item) { return min(decode_item(a, base, item).n_tiles, kSchedBuckets - 1); };
   for (int u = threadIdx.x; u < total; u += kSchedThreads) atomicAdd(&hist[bucket_of(u)], 1);
   __syncthreads();
-  {
-    constexpr int per = kSchedBuckets / kSchedThreads;
-    int local[per];
-    int sum = 0;
-#pragma unroll
-    for (int k = 0; k < per; ++k) {
-      local[k] = hist[kSchedBuckets - 1 - (threadIdx.x * per + k)];
-      sum += local[k];
-    }
-    int all;
-    int before = block_exclusive_scan(sum, warp_sums, all);
-#pragma unroll
-    for (int k = 0; k < per; ++k) {
-      hist[kSchedBuckets - 1 - (threadIdx.x * per + k)] = before;
-      before += local[k];
-    }
-  }
+  buckets_to_offsets_desc(hist, warp_sums);
   __syncthreads();
   for (int u = threadIdx.x; u < total; u += kSchedThreads) a.order[atomicAdd(&hist[bucket_of(u)], 1)] = u;
 }

@@ -49,7 +49,7 @@ def parse_args():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="chunked_prefill_16k",
                     choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "decode_16k", "decode_4k",
-                             "rope_16384", "kv_write_16384"])
+                             "rope_16384", "kv_write_16384", "split_combine_4k"])
     ap.add_argument("--splits", type=int, default=0, help="0 = automatic")
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="keep only the first N sequences of the workload (small cases for profiling)")
@@ -471,6 +471,67 @@ def kv_write_cpu_baseline(b, nbytes):
             "sample": "the full 16384-token write, 3 repetitions"}
 
 
+# --------------------------------------------------------------------- split-combine bench
+def combine_bench(args, world, rank, local):
+    """The cross-split reduce on the partials of the 4K chunked-prefill batch.
+
+    32768 query tokens x 16 heads x 128, ``--splits`` partials (default 4) in
+    bf16 with fp32 m/l, every split holding keys (l > 0), so every partial is
+    read: algorithmic bytes = S*T*H*(D*2 + 8) read + T*H*D*2 written (688 MB
+    at S = 4, larger than L2).
+    """
+    from minicpm_b200 import split_kv_combine
+
+    dev = torch.device("cuda", local)
+    s_count = args.splits if args.splits > 1 else 4
+    t, h, d = 32768, 16, 128
+    gen = torch.Generator().manual_seed(20260928)
+    o = torch.randn(s_count, t, h, d, generator=gen).to(torch.bfloat16).to(dev)
+    m = (torch.randn(s_count, t, h, generator=gen) * 3).to(dev)
+    l = (torch.rand(s_count, t, h, generator=gen) * 100 + 1).to(dev)
+    out = torch.empty(t, h, d, dtype=torch.bfloat16, device=dev)
+    nbytes = s_count * t * h * (d * 2 + 8) + t * h * d * 2
+
+    def step(i):
+        split_kv_combine(o, m, l, out)
+
+    for _ in range(args.warmup):
+        step(0)
+    ms, clocks = graph_timed(step, args.steps, local, world)
+    peaks, pkind = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        from oracle import split_kv_reduce_reference
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        n = 2048
+        oc, mc, lc = o[:, :n].float().cpu(), m[:, :n].cpu(), l[:, :n].cpu()
+        want = split_kv_reduce_reference(oc, mc, lc)
+        got = out[:n].float().cpu()
+        assert (got - want).abs().max().item() <= 2e-2, "combine differs from the oracle"
+        times = time_cpu(lambda: split_kv_reduce_reference(oc, mc, lc), 3)
+        cpu = {"value": nbytes * n / t / (sum(times) / len(times)) / 1e9, "unit": "GB/s",
+               "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"first {n} of {t} tokens, 3 repetitions (bytes scaled to the sample)"}
+    if rank == 0:
+        line = {
+            "metric": "Split-KV combine GB/s", "value": gbs * world, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "split_combine_4k", "tokens": t, "heads": h, "head_dim": d, "splits": s_count,
+                       "algorithmic_bytes": nbytes, "l2": "inputs larger than L2, back-to-back launches",
+                       "timing": "CUDA graph of all timed launches, replayed once"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": pkind},
+            "clocks": clocks,
+            "gpu_launches": args.steps,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------- verification
 def verify_sharded(args, batch, out, world, rank, splits):
     """Gather every rank's rows on rank 0 (NCCL) and compare them with one
@@ -503,6 +564,138 @@ def verify_sharded(args, batch, out, world, rank, splits):
     print(json.dumps({"verify_rows": int(full.shape[0]), "verify_bit_identical": same}), flush=True)
     if not same:
         raise SystemExit("sharded output differs from the single-GPU output")
+
+
+# --------------------------------------------------------------------- e2e (host buffers)
+E2E_MAX_GROUPS = 8
+E2E_MIN_SEQS_PER_GROUP = 4
+
+
+def split_into_groups(batch, n_groups: int):
+    """Contiguous groups of the batch's sequences, each a batch of its own.
+
+    Every group gets its own page pool holding exactly its sequences' pages,
+    placed by a seeded permutation inside the pool (the block table stays a
+    scattered physical mapping); Q rows, K/V values and lengths are the
+    batch's own, so each group's output rows equal the batch's.
+    """
+    from minicpm_b200.workloads import AttentionBatch
+
+    nseq = len(batch.query_lens)
+    bounds = [round(i * nseq / n_groups) for i in range(n_groups + 1)]
+    cu = batch.cu_seqlens_q.tolist()
+    bs = batch.kv_cache.shape[2]
+    parts = []
+    for gi in range(n_groups):
+        r0, r1 = bounds[gi], bounds[gi + 1]
+        if r0 == r1:
+            continue
+        pages = [math.ceil(L / bs) for L in batch.kv_lens[r0:r1]]
+        src = [batch.block_table[r, :n].long() for r, n in zip(range(r0, r1), pages)]
+        src = torch.cat(src) if sum(pages) else torch.empty(0, dtype=torch.long)
+        n = int(src.numel())
+        slot = torch.randperm(max(n, 1), generator=torch.Generator().manual_seed(7919 + gi))[:n]
+        pool = torch.zeros((max(n, 1),) + tuple(batch.kv_cache.shape[1:]), dtype=batch.kv_cache.dtype)
+        pool[slot] = batch.kv_cache[src]
+        table = torch.zeros(r1 - r0, max(max(pages), 1), dtype=torch.int32)
+        off = 0
+        for i, np_ in enumerate(pages):
+            table[i, :np_] = slot[off:off + np_].to(torch.int32)
+            off += np_
+        parts.append(AttentionBatch(
+            q=batch.q[cu[r0]:cu[r1]].contiguous(), kv_cache=pool, block_table=table,
+            cu_seqlens_q=torch.tensor([c - cu[r0] for c in cu[r0:r1 + 1]], dtype=torch.int32),
+            seqused_k=batch.seqused_k[r0:r1].clone(), query_lens=list(batch.query_lens[r0:r1]),
+            kv_lens=list(batch.kv_lens[r0:r1]), softmax_scale=batch.softmax_scale,
+            seq_ids=list(batch.seq_ids[r0:r1])))
+    return parts
+
+
+def e2e_pipelined(args, batch, out, splits, stream, world, total_flops, total_tokens):
+    """The metric through ``iluvatar_attention`` with host-resident inputs and output.
+
+    Each step copies every input from pinned host memory and reads ``out``
+    back, inside the timed region.  The batch's sequences go in up to eight
+    groups (at least four sequences each), each with its own page pool: group
+    i's host-to-device copies (one stream) overlap group i-1's attention call
+    (torch's current stream) and group i-2's read-back (a third stream), so
+    the step costs about the PCIe time of its bytes rather than the sum of
+    copies and compute.
+    """
+    from minicpm_b200 import iluvatar_attention
+
+    os.environ["ILUVATAR_USE_OPTIMIZED"] = "1"
+    os.environ["ILUVATAR_SPLIT_KV"] = "1"
+    os.environ["ILUVATAR_SPLIT_KV_DECODE"] = "1"  # a group of decode rows stays on the sm_100a kernels
+    if splits:
+        os.environ["ILUVATAR_NUM_SPLITS"] = str(splits)
+    dev = out.device
+    nseq = len(batch.query_lens)
+    n_groups = max(1, min(E2E_MAX_GROUPS, nseq // E2E_MIN_SEQS_PER_GROUP))
+    parts = split_into_groups(batch, n_groups)
+    keys = ("q", "kv_cache", "block_table", "cu_seqlens_q", "seqused_k")
+    host = [{k: getattr(p, k).pin_memory() for k in keys} for p in parts]
+    host_out = [torch.empty(p.q.shape, dtype=p.q.dtype).pin_memory() for p in parts]
+    dbuf = [{k: torch.empty(h[k].shape, dtype=h[k].dtype, device=dev) for k in keys} for h in host]
+    dout = [torch.empty(p.q.shape, dtype=p.q.dtype, device=dev) for p in parts]
+    h2d = sum(t.numel() * t.element_size() for h in host for t in h.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in parts]
+    ev_done = [torch.cuda.Event() for _ in parts]
+    ev_out = [torch.cuda.Event() for _ in parts]
+    for i in range(len(parts)):
+        ev_done[i].record(stream)
+        ev_out[i].record(stream)
+
+    def e2e_step():
+        for i, p in enumerate(parts):
+            h2d_s.wait_event(ev_done[i])  # the previous step's call has finished reading these buffers
+            with torch.cuda.stream(h2d_s):
+                for k in keys:
+                    dbuf[i][k].copy_(host[i][k], non_blocking=True)
+                ev_in[i].record(h2d_s)
+            stream.wait_event(ev_in[i])
+            stream.wait_event(ev_out[i])  # the previous step's read-back of dout[i] is done
+            d = dbuf[i]
+            iluvatar_attention(d["q"], d["kv_cache"], d["kv_cache"], dout[i], d["cu_seqlens_q"], p.max_seqlen_q,
+                               d["seqused_k"], p.max_seqlen_k, p.softmax_scale, causal=True,
+                               block_table=d["block_table"])
+            ev_done[i].record(stream)
+            d2h_s.wait_event(ev_done[i])
+            with torch.cuda.stream(d2h_s):
+                host_out[i].copy_(dout[i], non_blocking=True)
+                ev_out[i].record(d2h_s)
+        stream.wait_stream(d2h_s)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    h2d_s.wait_event(s)
+    d2h_s.wait_event(s)
+    for _ in range(args.steps):
+        e2e_step()
+    e.record(stream)
+    e.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(s.elapsed_time(e), world)
+    got = torch.cat(host_out) if host_out else torch.empty_like(out.cpu())
+    want = out.cpu()
+    identical = bool(torch.equal(got, want))
+    if not identical:
+        diff = (got.float() - want.float()).abs()
+        assert diff.max().item() <= 2e-2 and diff.mean().item() <= 1e-3, "e2e output differs from the device-resident run"
+    return {"value": total_flops * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": int(sum_over_ranks(float(h2d), world)),
+            "d2h_bytes_per_step": int(sum_over_ranks(float(d2h), world)),
+            "ms_per_step": e2e_ms / args.steps,
+            "tokens_per_s": total_tokens * args.steps / (e2e_ms * 1e-3),
+            "api": "iluvatar_attention, one call per sequence group",
+            "groups": len(parts), "overlap": "H2D of group i | attention of group i-1 | D2H of group i-2",
+            "bit_identical_to_device_run": identical}
 
 
 # --------------------------------------------------------------------- attention bench
@@ -577,45 +770,7 @@ def attention_bench(args, world, rank, local):
     # e2e: public operator API, host buffers, copies inside the timed region.
     e2e = None
     if not args.no_e2e:
-        os.environ["ILUVATAR_USE_OPTIMIZED"] = "1"
-        os.environ["ILUVATAR_SPLIT_KV"] = "1"
-        if splits:
-            os.environ["ILUVATAR_NUM_SPLITS"] = str(splits)
-        host = {k: getattr(batch, k).pin_memory() for k in ("q", "kv_cache", "block_table", "cu_seqlens_q", "seqused_k")}
-        host_out = torch.empty(batch.q.shape, dtype=batch.q.dtype).pin_memory()
-        dq = torch.empty_like(g.q)
-        dkv = torch.empty_like(g.kv_cache)
-        dbt, dcu, dsu = torch.empty_like(g.block_table), torch.empty_like(g.cu_seqlens_q), torch.empty_like(g.seqused_k)
-        dout = torch.empty_like(g.q)
-        h2d = sum(t.numel() * t.element_size() for t in host.values())
-        d2h = host_out.numel() * host_out.element_size()
-
-        def e2e_step():
-            dq.copy_(host["q"], non_blocking=True)
-            dkv.copy_(host["kv_cache"], non_blocking=True)
-            dbt.copy_(host["block_table"], non_blocking=True)
-            dcu.copy_(host["cu_seqlens_q"], non_blocking=True)
-            dsu.copy_(host["seqused_k"], non_blocking=True)
-            iluvatar_attention(dq, dkv, dkv, dout, dcu, batch.max_seqlen_q, dsu, batch.max_seqlen_k,
-                               batch.softmax_scale, causal=True, block_table=dbt)
-            host_out.copy_(dout, non_blocking=True)
-
-        e2e_step()
-        barrier(world)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        e.record(stream)
-        e.synchronize()
-        barrier(world)
-        e2e_ms = max_over_ranks(s.elapsed_time(e), world)
-        e2e = {"value": total_flops * args.steps / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": int(sum_over_ranks(float(h2d), world)),
-               "d2h_bytes_per_step": int(sum_over_ranks(float(d2h), world)),
-               "ms_per_step": e2e_ms / args.steps,
-               "tokens_per_s": total_tokens * args.steps / (e2e_ms * 1e-3)}
-        assert torch.equal(host_out, out.cpu()), "e2e output differs from the device-resident run"
+        e2e = e2e_pipelined(args, batch, out, splits, stream, world, total_flops, total_tokens)
 
     if args.verify:
         verify_sharded(args, batch, out, world, rank, splits)
@@ -714,6 +869,8 @@ def main():
             rope_bench(args, world, rank, local)
         elif args.workload == "kv_write_16384":
             kv_write_bench(args, world, rank, local)
+        elif args.workload == "split_combine_4k":
+            combine_bench(args, world, rank, local)
         else:
             attention_bench(args, world, rank, local)
     finally:

@@ -333,11 +333,15 @@ int b200_split_combine(const B200CombineParams* p, void* stream) {
   const dim3 grid((unsigned)((rows + rows_per_block - 1) / rows_per_block));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-#define B200_COMBINE_D(TO, TOUT)                                                                   \
-  switch (p->head_dim) {                                                                          \
-    case 64: b200::split_combine_kernel<TO, TOUT, 64><<<grid, b200::kCombineThreads, 0, s>>>(a); break;   \
-    case 128: b200::split_combine_kernel<TO, TOUT, 128><<<grid, b200::kCombineThreads, 0, s>>>(a); break; \
-    default: b200::split_combine_kernel<TO, TOUT, 256><<<grid, b200::kCombineThreads, 0, s>>>(a); break;  \
+#define B200_COMBINE_S(TO, TOUT, D)                                                                      \
+  if (p->num_splits <= 4) b200::split_combine_kernel<TO, TOUT, D, 4><<<grid, b200::kCombineThreads, 0, s>>>(a);      \
+  else if (p->num_splits <= 8) b200::split_combine_kernel<TO, TOUT, D, 8><<<grid, b200::kCombineThreads, 0, s>>>(a); \
+  else b200::split_combine_kernel<TO, TOUT, D, 16><<<grid, b200::kCombineThreads, 0, s>>>(a);
+#define B200_COMBINE_D(TO, TOUT)                         \
+  switch (p->head_dim) {                                \
+    case 64: B200_COMBINE_S(TO, TOUT, 64) break;         \
+    case 128: B200_COMBINE_S(TO, TOUT, 128) break;       \
+    default: B200_COMBINE_S(TO, TOUT, 256) break;        \
   }
 #define B200_COMBINE_OUT(TO)                                                            \
   switch (p->out_dtype) {                                                               \
@@ -354,6 +358,7 @@ int b200_split_combine(const B200CombineParams* p, void* stream) {
   }
 #undef B200_COMBINE_OUT
 #undef B200_COMBINE_D
+#undef B200_COMBINE_S
   return check_launch("split_combine_kernel");
 }
 

@@ -3,10 +3,11 @@
 // Follows _split_kv_reduce (kernels/triton_split_kv_paged.py:197-228 of the
 // reference project): m* = max_s m_s; w_s = exp(m_s - m*) * l_s when l_s > 0,
 // else 0; out = sum_s w_s O_s / max(sum_s w_s, 1e-20).  A split with
-// l_s == 0 is never read (the reference multiplies it by 0).
+// l_s == 0 contributes nothing (the reference multiplies it by 0; here it
+// is selected out, so even a NaN there cannot reach the output).
 //
 // Bandwidth kernel: one (token, head) row per group of D/8 threads, each
-// thread moving 8 elements with 16-byte loads and stores.
+// thread moving 8 elements of every split with 16-byte loads and stores.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -93,7 +94,50 @@ __device__ __forceinline__ void store8<__half>(__half* p, const float (&v)[8]) {
   *reinterpret_cast<uint4*>(p) = w;
 }
 
-template <typename TO, typename TOut, int D>
+// Raw 16-byte pieces of one row chunk of 8 elements (one piece for 16-bit
+// types, two for fp32), loaded with the streaming hint: partials are read once.
+template <typename T>
+struct SplitChunk8 {
+  static constexpr int kPieces = sizeof(T) == 4 ? 2 : 1;
+  uint4 w[kPieces];
+  __device__ __forceinline__ void load(const T* p) {
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) w[i] = __ldcs(reinterpret_cast<const uint4*>(p) + i);
+  }
+  __device__ __forceinline__ void to_float(float (&v)[8]) const;
+};
+template <>
+__device__ __forceinline__ void SplitChunk8<float>::to_float(float (&v)[8]) const {
+  v[0] = __uint_as_float(w[0].x); v[1] = __uint_as_float(w[0].y); v[2] = __uint_as_float(w[0].z); v[3] = __uint_as_float(w[0].w);
+  v[4] = __uint_as_float(w[1].x); v[5] = __uint_as_float(w[1].y); v[6] = __uint_as_float(w[1].z); v[7] = __uint_as_float(w[1].w);
+}
+template <>
+__device__ __forceinline__ void SplitChunk8<__nv_bfloat16>::to_float(float (&v)[8]) const {
+  const uint32_t u[4] = {w[0].x, w[0].y, w[0].z, w[0].w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void SplitChunk8<__half>::to_float(float (&v)[8]) const {
+  const uint32_t u[4] = {w[0].x, w[0].y, w[0].z, w[0].w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// One (token, head) row per D/8 threads, up to kS splits (kS = 4, 8 or 16,
+// the smallest bound >= num_splits).  Every load of a row -- the partial
+// O chunks of all splits and the m / l values -- is issued before any is
+// used, so a row costs one memory round trip; a split with l = 0 is then
+// left out by selection (its O, whatever it holds, never reaches the sum).
+template <typename TO, typename TOut, int D, int kS>
 __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const CombineArgs a) {
   constexpr int kThreadsPerRow = D / 8;
   constexpr int kRowsPerBlock = kCombineThreads / kThreadsPerRow;
@@ -104,28 +148,32 @@ __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const Co
   const int64_t t = row / a.num_heads;
   const int64_t h = row - t * a.num_heads;
 
-  float mv[kMaxSplits], lv[kMaxSplits];
-  float m_max = -INFINITY;
+  const TO* o = static_cast<const TO*>(a.o) + t * a.o_st + h * a.o_sh + d0;
+  SplitChunk8<TO> raw[kS];
+  float mv[kS], lv[kS];
 #pragma unroll
-  for (int s = 0; s < kMaxSplits; ++s) {
+  for (int s = 0; s < kS; ++s)
+    if (s < a.num_splits) raw[s].load(o + s * a.o_ss);
+#pragma unroll
+  for (int s = 0; s < kS; ++s) {
+    mv[s] = -INFINITY;
+    lv[s] = 0.f;
     if (s < a.num_splits) {
-      mv[s] = a.m[s * a.m_ss + t * a.m_st + h * a.m_sh];
-      lv[s] = a.l[s * a.l_ss + t * a.l_st + h * a.l_sh];
-      m_max = fmaxf(m_max, mv[s]);
-    } else {
-      mv[s] = -INFINITY;
-      lv[s] = 0.f;
+      mv[s] = __ldg(a.m + s * a.m_ss + t * a.m_st + h * a.m_sh);
+      lv[s] = __ldg(a.l + s * a.l_ss + t * a.l_st + h * a.l_sh);
     }
   }
+  float m_max = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < kS; ++s) m_max = fmaxf(m_max, mv[s]);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float denom = 0.f;
-  const TO* o = static_cast<const TO*>(a.o) + t * a.o_st + h * a.o_sh + d0;
 #pragma unroll
-  for (int s = 0; s < kMaxSplits; ++s) {
+  for (int s = 0; s < kS; ++s) {
     if (s < a.num_splits && lv[s] > 0.f) {
       const float w = expf(mv[s] - m_max) * lv[s];
       float v[8];
-      load8<TO>(o + s * a.o_ss, v);
+      raw[s].to_float(v);
       denom += w;
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, v[i], acc[i]);

@@ -89,8 +89,8 @@ enum : int {
   BAR_KV_FULL = 2,                           // + slot
   BAR_KV_EMPTY = BAR_KV_FULL + kKvStages,    // + slot
   BAR_S_FULL = BAR_KV_EMPTY + kKvStages,     // + tile
-  BAR_P_FULL = BAR_S_FULL + 2,               // + 4 * tile + quarter (32 keys of P)
-  BAR_O_DONE = BAR_P_FULL + 8,               // + tile
+  BAR_P_FULL = BAR_S_FULL + 2,               // + 2 * tile + half (64 keys of P)
+  BAR_O_DONE = BAR_P_FULL + 4,               // + tile
   BAR_IT_FULL = BAR_O_DONE + 2,              // + ring entry
   BAR_IT_EMPTY = BAR_IT_FULL + kUnitRing,    // + ring entry
   BAR_DRAIN = BAR_IT_EMPTY + kUnitRing,
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(BAR_S_FULL + t), 1);
-      for (int q = 0; q < 4; ++q) mbar_init(bar(BAR_P_FULL + 4 * t + q), 4);
+      for (int h = 0; h < 2; ++h) mbar_init(bar(BAR_P_FULL + 2 * t + h), 4);
       mbar_init(bar(BAR_O_DONE + t), 1);
     }
     for (int r = 0; r < kUnitRing; ++r) {
@@ -416,29 +416,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       constexpr uint32_t idesc_pv = umma_idesc_f16(kBF16, 128, 128, false, true);
       int fills = 0, q_uses = 0;
       int tiles_done[2] = {0, 0};  // tiles already processed by query-tile group t
+      // Descriptors are built once per operand tile; the UMMAs of a tile step
+      // their start address by adding (offset >> 4) to the descriptor's
+      // address field (shared addresses stay below 256 KB, so the 14-bit field
+      // never carries).  Every instruction between two UMMAs idles the tensor
+      // core, which takes only about one UMMA ahead of execution.
       auto issue_s = [&](int t, uint32_t kslot_addr) {
-        const uint32_t q = sbase + kSmQ + t * 32768;
+        const uint64_t qd = umma_desc_sw128(sbase + kSmQ + t * 32768, 16, 1024);
+        const uint64_t kd = umma_desc_sw128(kslot_addr, 16, kHeadMaps ? 2048 : 1024);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t qoff = (kk >> 2) * 16384 + (kk & 3) * 32;
           const uint32_t koff = kv_slot_offset<kHeadMaps>(0, kk >> 2, 0) + (kk & 3) * 32;
-          umma_ss(tmem + t * 128, umma_desc_sw128(q + qoff, 16, 1024),
-                  umma_desc_sw128(kslot_addr + koff, 16, kHeadMaps ? 2048 : 1024), idesc_qk, kk > 0);
+          umma_ss(tmem + t * 128, qd + (qoff >> 4), kd + (koff >> 4), idesc_qk, kk > 0);
         }
         tc_commit(bar(BAR_S_FULL + t));
       };
       auto issue_pv = [&](int t, int c, uint32_t vslot_addr, bool acc) {
+        const uint64_t vd = umma_desc_sw128(vslot_addr, kHeadMaps ? 1024 : 16384, kHeadMaps ? 2048 : 1024);
         for (int q = 0; q < 4; ++q) {
-          if (!mbar_wait(bar(BAR_P_FULL + 4 * t + q), c & 1, abort_flag)) return false;
-          tc_fence_after();
+          if (q % 2 == 0) {  // P is published in halves of 64 keys
+            if (!mbar_wait(bar(BAR_P_FULL + 2 * t + q / 2), c & 1, abort_flag)) return false;
+            tc_fence_after();
+          }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int kk = 2 * q + h;
             // V is the MN-major B operand: 64-column atoms at LBO, 8-key groups at SBO.
             umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                    umma_desc_sw128(vslot_addr + kv_slot_offset<kHeadMaps>(16 * kk, 0, 0), kHeadMaps ? 1024 : 16384,
-                                    kHeadMaps ? 2048 : 1024),
-                    idesc_pv, (acc || kk > 0) ? 1u : 0u);
+                    vd + (kv_slot_offset<kHeadMaps>(16 * kk, 0, 0) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
           }
         }
         tc_commit(bar(BAR_O_DONE + t));
@@ -638,10 +644,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             pk[i] = Pack2<T>::pack(p0, p1);
           }
           tmem_st16(s_addr + 16 * c4, pk);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(BAR_P_FULL + 4 * t + c4));  // one arrival per softmax warp
+          if (c4 % 2 == 1) {  // publish P in halves: two waits for the issuer per tile instead of four
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(BAR_P_FULL + 2 * t + c4 / 2));  // one arrival per softmax warp
+          }
         }
         {
           float a0, a1;

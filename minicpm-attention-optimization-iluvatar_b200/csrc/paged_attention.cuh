@@ -432,7 +432,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         tc_commit(bar(BAR_S_FULL + t));
       };
-      auto issue_pv = [&](int t, int c, uint32_t vslot_addr, bool acc) {
+      auto issue_pv = [&](int t, int c, uint32_t vslot_addr, bool acc, bool last) {
         const uint64_t vd = umma_desc_sw128(vslot_addr, kHeadMaps ? 1024 : 16384, kHeadMaps ? 2048 : 1024);
         for (int q = 0; q < 4; ++q) {
           if (q % 2 == 0) {  // P is published in halves of 64 keys
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     vd + (kv_slot_offset<kHeadMaps>(16 * kk, 0, 0) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
           }
         }
-        tc_commit(bar(BAR_O_DONE + t));
+        if (last) tc_commit(bar(BAR_O_DONE + t));  // the epilogue's wait; earlier tiles need none
         return true;
       };
       auto slot_addr = [&](int g) { return sbase + kSmKV + (g % kKvStages) * 32768; };
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int j = 0; ok && j < n_tiles; ++j) {
           const int vidx = fills + 2 * j + 1, kidx = fills + 2 * j + 2;
           const bool more = j + 1 < n_tiles;
-          if (!wait_full(vidx) || !issue_pv(0, tiles_done[0] + j, slot_addr(vidx), j > 0)) {
+          if (!wait_full(vidx) || !issue_pv(0, tiles_done[0] + j, slot_addr(vidx), j > 0, !more)) {
             ok = false;
             break;
           }
@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             issue_s(0, slot_addr(kidx));
           }
           if (two) {
-            if (!issue_pv(1, tiles_done[1] + j, slot_addr(vidx), j > 0)) {
+            if (!issue_pv(1, tiles_done[1] + j, slot_addr(vidx), j > 0, !more)) {
               ok = false;
               break;
             }
@@ -519,6 +519,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float sl2 = a.scale_log2;
     int fills = 0;       // K/V ring fills of the units before this one
     int tiles_done = 0;  // tiles this group processed in earlier units
+    int o_units = 0;     // O_DONE phases seen: one per unit with tiles for this group
     bool aborted = false;
     for (int it = 0; !aborted; ++it) {
       UnitEntry e;
@@ -588,12 +589,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (__any_sync(0xffffffffu, raise)) {
           const float alpha = raise ? ex2_approx(m_used - m_cand) : 1.f;  // 0 when m_used = -inf
           if (j > 0) {
-            // O holds PV of tiles < j: scale it before PV_j accumulates.
-            if (!mbar_wait(bar(BAR_O_DONE + t), (c - 1) & 1, abort_flag)) {
-              aborted = true;
-              break;
-            }
-            tc_fence_after();
+            // O holds PV of tiles < j: scale it before PV_j accumulates.  The
+            // S_FULL phase of tile j already implies PV_{j-1} is complete: its
+            // commit covers every UMMA the issuer started before S_j.
 #pragma unroll 1
             for (int c8 = 0; c8 < 8; ++c8) {
               uint32_t o[16];
@@ -660,8 +658,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
       // ---------------------------------------------------------- epilogue
       if (!aborted && n_tiles > 0) {
-        if (!mbar_wait(bar(BAR_O_DONE + t), (tiles_done + n_tiles - 1) & 1, abort_flag)) aborted = true;
+        if (!mbar_wait(bar(BAR_O_DONE + t), o_units & 1, abort_flag)) aborted = true;
         tc_fence_after();
+        ++o_units;
       }
       tiles_done += n_tiles;
       if (aborted) break;

@@ -135,54 +135,70 @@ __device__ __forceinline__ void SplitChunk8<__half>::to_float(float (&v)[8]) con
 // One (token, head) row per D/8 threads, up to kS splits (kS = 4, 8 or 16,
 // the smallest bound >= num_splits).  Every load of a row -- the partial
 // O chunks of all splits and the m / l values -- is issued before any is
-// used, so a row costs one memory round trip; a split with l = 0 is then
-// left out by selection (its O, whatever it holds, never reaches the sum).
+// used, so a row costs one memory round trip.  The m / l values of a row are
+// loaded once per row group (thread j of the group holds splits j, j + D/8,
+// ...), the group reduces the maximum and forms each split's weight, and the
+// weights reach every thread of the group by shuffles.  A split with l = 0
+// carries weight -1 and is left out by selection (its O, whatever it holds,
+// never reaches the sum).
 template <typename TO, typename TOut, int D, int kS>
 __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const CombineArgs a) {
   constexpr int kThreadsPerRow = D / 8;
   constexpr int kRowsPerBlock = kCombineThreads / kThreadsPerRow;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / kThreadsPerRow;
-  const int d0 = (threadIdx.x % kThreadsPerRow) * 8;
+  constexpr int kPer = (kS + kThreadsPerRow - 1) / kThreadsPerRow;  // splits whose m / l one thread loads
+  const int sub = threadIdx.x % kThreadsPerRow;
   const int64_t nrows = static_cast<int64_t>(a.total_q) * a.num_heads;
-  if (row >= nrows) return;
+  const int64_t row_raw = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / kThreadsPerRow;
+  const bool valid = row_raw < nrows;  // threads past the end still take part in the shuffles
+  const int64_t row = valid ? row_raw : nrows - 1;
   const int64_t t = row / a.num_heads;
   const int64_t h = row - t * a.num_heads;
+  const int d0 = sub * 8;
 
   const TO* o = static_cast<const TO*>(a.o) + t * a.o_st + h * a.o_sh + d0;
   SplitChunk8<TO> raw[kS];
-  float mv[kS], lv[kS];
 #pragma unroll
   for (int s = 0; s < kS; ++s)
     if (s < a.num_splits) raw[s].load(o + s * a.o_ss);
+  float mk[kPer], lk[kPer];
 #pragma unroll
-  for (int s = 0; s < kS; ++s) {
-    mv[s] = -INFINITY;
-    lv[s] = 0.f;
+  for (int k = 0; k < kPer; ++k) {
+    const int s = sub + k * kThreadsPerRow;
+    mk[k] = -INFINITY;
+    lk[k] = 0.f;
     if (s < a.num_splits) {
-      mv[s] = __ldg(a.m + s * a.m_ss + t * a.m_st + h * a.m_sh);
-      lv[s] = __ldg(a.l + s * a.l_ss + t * a.l_st + h * a.l_sh);
+      mk[k] = __ldg(a.m + s * a.m_ss + t * a.m_st + h * a.m_sh);
+      lk[k] = __ldg(a.l + s * a.l_ss + t * a.l_st + h * a.l_sh);
     }
   }
-  float m_max = -INFINITY;
+  float m_max = mk[0];
 #pragma unroll
-  for (int s = 0; s < kS; ++s) m_max = fmaxf(m_max, mv[s]);
+  for (int k = 1; k < kPer; ++k) m_max = fmaxf(m_max, mk[k]);
+#pragma unroll
+  for (int off = kThreadsPerRow / 2; off > 0; off >>= 1)
+    m_max = fmaxf(m_max, __shfl_xor_sync(0xffffffffu, m_max, off, kThreadsPerRow));
+  float wk[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) wk[k] = lk[k] > 0.f ? expf(mk[k] - m_max) * lk[k] : -1.f;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float denom = 0.f;
 #pragma unroll
   for (int s = 0; s < kS; ++s) {
-    if (s < a.num_splits && lv[s] > 0.f) {
-      const float w = expf(mv[s] - m_max) * lv[s];
-      float v[8];
-      raw[s].to_float(v);
-      denom += w;
+    if (s < a.num_splits) {
+      const float w = __shfl_sync(0xffffffffu, wk[s / kThreadsPerRow], s % kThreadsPerRow, kThreadsPerRow);
+      if (w >= 0.f) {
+        float v[8];
+        raw[s].to_float(v);
+        denom += w;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, v[i], acc[i]);
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(w, v[i], acc[i]);
+      }
     }
   }
   const float inv = 1.f / fmaxf(denom, 1e-20f);
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] *= inv;
-  store8<TOut>(static_cast<TOut*>(a.out) + t * a.out_st + h * a.out_sh + d0, acc);
+  if (valid) store8<TOut>(static_cast<TOut*>(a.out) + t * a.out_st + h * a.out_sh + d0, acc);
 }
 
 }  // namespace b200

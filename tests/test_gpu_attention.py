@@ -207,3 +207,34 @@ def test_split_combine_matches_reference_reduce(golden_dir):
         out16 = torch.empty(o.shape[1:], device="cuda", dtype=torch.bfloat16)
         split_kv_combine(o.to(torch.bfloat16), m, l, out16)
         assert (out16.cpu().float() - want).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("head_dim", [64, 128, 256])
+@pytest.mark.parametrize("num_splits", [1, 2, 3, 5, 8, 13, 16])
+@pytest.mark.parametrize("partial_dtype", [torch.float32, torch.bfloat16])
+def test_split_combine_shapes_against_oracle(head_dim, num_splits, partial_dtype):
+    """The combine over every split bound (4 / 8 / 16) and row-group width
+    (head_dim / 8 threads per row), with inactive splits holding NaN, rows
+    with no active split, and a row count that leaves a partial block."""
+    from oracle import split_kv_reduce_reference
+
+    gen = torch.Generator().manual_seed(1000 * head_dim + num_splits)
+    t, h = 37, 3  # 111 rows: not a multiple of any block's row count
+    o = torch.randn(num_splits, t, h, head_dim, generator=gen)
+    m = torch.randn(num_splits, t, h, generator=gen) * 4
+    l = torch.rand(num_splits, t, h, generator=gen) * 50 + 0.5
+    inactive = torch.rand(num_splits, t, h, generator=gen) < 0.3
+    inactive[:, 5, 1] = True  # a row with no active split at all
+    l[inactive] = 0.0
+    m[inactive] = float("-inf")
+    o[inactive] = float("nan")
+    want = split_kv_reduce_reference(o, m, l)
+    out_dtype = torch.float32 if partial_dtype == torch.float32 else torch.bfloat16
+    out = torch.empty(t, h, head_dim, device="cuda", dtype=out_dtype)
+    split_kv_combine(o.to(partial_dtype).cuda(), m.cuda(), l.cuda(), out)
+    torch.cuda.synchronize()
+    got = out.float().cpu()
+    assert torch.isfinite(got).all()
+    assert torch.equal(got[5, 1], torch.zeros(head_dim))
+    tol = 2e-5 if partial_dtype == torch.float32 else 2e-2
+    assert (got - want).abs().max().item() <= tol

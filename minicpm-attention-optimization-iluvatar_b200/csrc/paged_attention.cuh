@@ -73,6 +73,7 @@ static_assert(kAttnProducerRegs + 2 * kAttnSoftmaxRegs == 3 * kAttnLaunchRegs, "
 constexpr int kAttnTmemCols = 512;
 constexpr int kKvStages = 5;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 2^8
+constexpr float kRescaleSum = 256.0f;      // 2^kRescaleThreshold
 
 // Shared memory map (offsets from a 1024-aligned base).
 constexpr uint32_t kSmQ = 0;                            // Q0, Q1: 2 x (2 x 16 KB)
@@ -573,9 +574,52 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               if (col < lo || col >= hi) sr[c4][cc] = __float_as_uint(-INFINITY);
             }
         }
+        // Fast path: when the second half's maximum stays within the rescale
+        // threshold of the running maximum, the first half's P is computed
+        // against the running maximum at once and checked by its sum (a sum of
+        // at most 2^threshold bounds every element the same way), so the
+        // first half's maximum pass is skipped.  Any failure in the warp falls
+        // back to the full pass, which overwrites the speculative P in TMEM
+        // before anything is published; results are identical either way.
+        const uint64_t sl2_2 = f2_pack(sl2, sl2);
+        uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
+        bool fast = false;
+        {
+          float m1[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int c4 = 2; c4 < 4; ++c4)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+                m1[k] = fmax3(m1[k], __uint_as_float(sr[c4][8 * h + 2 * k]), __uint_as_float(sr[c4][8 * h + 2 * k + 1]));
+          const float mh1 = fmaxf(fmaxf(m1[0], m1[1]), fmaxf(m1[2], m1[3])) * sl2;
+          if (__all_sync(0xffffffffu, m_used != -INFINITY && mh1 <= m_used + kRescaleThreshold)) {
+            const uint64_t negm_2 = f2_pack(-m_used, -m_used);
+#pragma unroll
+            for (int c4 = 0; c4 < 2; ++c4) {
+              uint32_t pk[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[c4][2 * i]), __uint_as_float(sr[c4][2 * i + 1])), sl2_2, negm_2);
+                float x0, x1;
+                f2_unpack(x2, x0, x1);
+                const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+                if (i & 1) sum_b = f2_add(sum_b, f2_pack(p0, p1)); else sum_a = f2_add(sum_a, f2_pack(p0, p1));
+                pk[i] = Pack2<T>::pack(p0, p1);
+              }
+              tmem_st16(s_addr + 16 * c4, pk);
+            }
+            float a0, a1;
+            f2_unpack(f2_add(sum_a, sum_b), a0, a1);
+            fast = __all_sync(0xffffffffu, a0 + a1 <= kRescaleSum);
+            if (!fast) sum_a = sum_b = f2_pack(0.f, 0.f);
+          }
+        }
         float mx[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+        if (!fast) {
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4)
 #pragma unroll
@@ -607,6 +651,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             m_used = m_cand;
           }
         }
+        }  // !fast
         const float neg_m = (m_used == -INFINITY) ? 0.f : -m_used;
         if (t == 0 && j == n_tiles - 1 && v_tail_from < v_tail_to) {
           // Rows of the last page past the sequence end may hold anything (NaN
@@ -627,11 +672,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           fence_proxy_async_smem();
         }
 
-        const uint64_t sl2_2 = f2_pack(sl2, sl2), negm_2 = f2_pack(neg_m, neg_m);
-        uint64_t sum_a = f2_pack(0.f, 0.f), sum_b = sum_a;
+        const uint64_t negm_2 = f2_pack(neg_m, neg_m);
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t pk[16];
+          if (!(fast && c4 < 2)) {  // the fast path has stored quarters 0 and 1 already
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sr[c4][2 * i]), __uint_as_float(sr[c4][2 * i + 1])), sl2_2, negm_2);
@@ -642,6 +687,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             pk[i] = Pack2<T>::pack(p0, p1);
           }
           tmem_st16(s_addr + 16 * c4, pk);
+          }
           if (c4 % 2 == 1) {  // publish P in halves: two waits for the issuer per tile instead of four
             tmem_wait_st();
             tc_fence_before();

@@ -302,7 +302,7 @@ size_t b200_attn_workspace_bytes(int32_t total_q, int32_t num_seqs, int32_t num_
   const int elt = (dtype == B200_DTYPE_F32) ? 4 : 2;
   size_t bytes = attn_workspace_layout(total_q, num_seqs, num_q_heads, num_kv_heads, head_dim, num_splits, elt).total;
   // A batch with at most one query token per sequence may run the decode kernel.
-  if (total_q <= num_seqs && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0 &&
+  if (total_q <= num_seqs && num_kv_heads > 0 && num_q_heads % num_kv_heads == 0 && head_dim == b200::kAttnHeadDim &&
       decode_shape_ok(num_q_heads / num_kv_heads, num_kv_heads))
     bytes = std::max(bytes, decode_layout(num_seqs, num_kv_heads, num_q_heads / num_kv_heads, max_seqlen_k,
                                           sm_count()).total);
@@ -371,8 +371,12 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   if (p->block_size <= 0 || p->block_size % 16) return fail(B200_ERR_INVALID, "unsupported head shape for paged Split-KV");
   if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256)
     return fail(B200_ERR_INVALID, "unsupported head shape for paged Split-KV");
-  if (p->head_dim != b200::kAttnHeadDim)
-    return fail(B200_ERR_UNSUPPORTED, "head_dim %d: the sm_100a kernel is built for head_dim 128", p->head_dim);
+  // head_dim 64 runs the head_dim-128 kernel: the tensor maps describe the
+  // real 64-element rows, so the second 64-column half of every Q, K and V
+  // box lies outside them and TMA fills it with zeros; S and P V are then
+  // exactly those of head_dim 64, and the epilogue stores 64 columns.
+  if (p->head_dim != b200::kAttnHeadDim && p->head_dim != 64)
+    return fail(B200_ERR_UNSUPPORTED, "head_dim %d: the sm_100a kernel handles head_dim 64 and 128", p->head_dim);
   const int group = p->num_q_heads / p->num_kv_heads;
   if (group > b200::kAttnTileM || b200::kAttnTileM % group)
     return fail(B200_ERR_UNSUPPORTED, "query heads per KV head (%d) must divide 128", group);
@@ -393,7 +397,8 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
        elt) & 15)
     return fail(B200_ERR_UNSUPPORTED, "token/head/block strides must be multiples of 16 bytes");
   // Decode batches take the decode kernel (its own workspace layout and maps).
-  if (p->max_seqlen_q == 1 && decode_shape_ok(group, p->num_kv_heads) && use_decode_kernel())
+  if (p->max_seqlen_q == 1 && p->head_dim == b200::kAttnHeadDim && decode_shape_ok(group, p->num_kv_heads) &&
+      use_decode_kernel())
     return run_decode(p, static_cast<cudaStream_t>(stream), group);
 
   const int splits = p->num_splits > 0 ? p->num_splits
@@ -430,8 +435,9 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // CTA-pair kernel (M = 256 UMMA across two SMs) or single-CTA kernel; the
   // single-CTA kernel takes per-KV-head maps (4 KB boxes) when they fit.
-  const bool pair = use_cta_pair();
-  const bool head_maps = !pair && p->num_kv_heads <= b200::kMaxHeadMaps;
+  // Per-KV-head maps and the CTA-pair kernel assume full 128-column rows.
+  const bool pair = use_cta_pair() && p->head_dim == b200::kAttnHeadDim;
+  const bool head_maps = !pair && p->num_kv_heads <= b200::kMaxHeadMaps && p->head_dim == b200::kAttnHeadDim;
   b200::KvHeadMaps maps;
   if (head_maps) {
     if (int r = encode_kv_head_maps(p, dt, &maps)) return r;
@@ -480,6 +486,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   a.block_size = p->block_size;
   a.num_blocks = p->num_blocks;
   a.num_splits = splits;
+  a.head_dim = p->head_dim;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
   // Upper bound on work units for this unit size (surplus CTAs of the pair

@@ -128,6 +128,7 @@ struct AttnKernelArgs {
   int block_size;
   int num_blocks;
   int num_splits;
+  int head_dim;       // 128, or 64 (the upper 64 columns of every tile are TMA zero fill)
   float scale_log2;   // softmax_scale * log2(e)
 };
 
@@ -717,7 +718,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         dst = static_cast<T*>(a.out) + static_cast<int64_t>(tok) * a.out_st + static_cast<int64_t>(row_head) * a.out_sh;
       } else {
         const int64_t rowi = (static_cast<int64_t>(e.split) * a.total_q + tok) * a.num_q_heads + row_head;
-        dst = static_cast<T*>(a.o_split) + rowi * kAttnHeadDim;
+        dst = static_cast<T*>(a.o_split) + rowi * a.head_dim;
         if (row_valid) {
           a.m_split[rowi] = (l > 0.f) ? m_used * 0.69314718055994530942f : -INFINITY;
           a.l_split[rowi] = l;
@@ -725,6 +726,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
+        if (c4 * 32 >= a.head_dim) break;  // warp-uniform: only the row's real columns
         uint32_t o[32];
         if (n_tiles > 0) {
           tmem_ld32(o_addr + 32 * c4, o);

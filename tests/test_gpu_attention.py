@@ -238,3 +238,32 @@ def test_split_combine_shapes_against_oracle(head_dim, num_splits, partial_dtype
     assert torch.equal(got[5, 1], torch.zeros(head_dim))
     tol = 2e-5 if partial_dtype == torch.float32 else 2e-2
     assert (got - want).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 2), (8, 8), (16, 1)])
+def test_head_dim_64_against_oracle(hq, hkv):
+    """head_dim 64 (accepted by the reference wrapper): the head_dim-128 kernel
+    with the upper half of every Q/K/V box zero-filled by TMA, 64 columns
+    stored; partial pages, a decode row, splits 1 / 4 / auto."""
+    batch = small_batch([37, 1, 100, 16], [200, 63, 1000, 0], seed=64, num_q_heads=hq, num_kv_heads=hkv, head_dim=64)
+    want = oracle(batch)
+    for s in (1, 4, 0):
+        assert_close(run_gpu(batch, s), want, f"d64 {hq}/{hkv} S={s}")
+    _no_device_error()
+
+
+def test_head_dim_64_decode_batch_and_dispatcher(monkeypatch):
+    """A head_dim-64 batch of decode rows takes the prefill kernel (the decode
+    kernel is built for 128); through the dispatcher with the 5-D cache."""
+    batch = small_batch([1, 1, 1], [5, 700, 2048], seed=65, head_dim=64)
+    assert_close(run_gpu(batch, 0), oracle(batch), "d64 decode rows")
+    b = small_batch([20, 33], [100, 400], seed=66, head_dim=64).to("cuda")
+    out = torch.empty_like(b.q)
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    iluvatar_attention(b.q, b.kv_cache, b.kv_cache, out, b.cu_seqlens_q, b.max_seqlen_q, b.seqused_k, b.max_seqlen_k,
+                       b.softmax_scale, causal=True, block_table=b.block_table)
+    torch.cuda.synchronize()
+    cpu = small_batch([20, 33], [100, 400], seed=66, head_dim=64)
+    assert_close(out.cpu(), oracle(cpu), "d64 dispatcher")
+    _no_device_error()

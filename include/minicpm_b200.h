@@ -146,6 +146,19 @@ B200_API int32_t b200_choose_num_splits(int32_t total_q, int32_t num_seqs, int32
 B200_API int b200_paged_attn_fwd(const B200AttnParams* params, void* stream);
 
 /*
+ * 1 if b200_paged_attn_fwd runs this head shape and element type, else 0:
+ * q/k/v/out F16 or BF16, head_dim 64 or 128, num_q_heads a multiple of
+ * num_kv_heads with at most 128 query heads per KV head.  The dispatcher and
+ * the service route other shapes to their baseline kernel before calling in,
+ * as they route the unsupported features of kernels/attention.py:99-110 and
+ * integration/vllm-plugin-FL-split-kv.patch:88-141 (the reference's Triton
+ * kernel takes head_dim 64/128/256 and any ratio,
+ * kernels/triton_split_kv_paged.py:270-279).
+ */
+B200_API int32_t b200_attn_shape_supported(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                           int32_t dtype);
+
+/*
  * b200_paged_attn_fwd without a caller-supplied workspace: no counterpart in
  * the reference.  For callers that cannot allocate device memory at call time
  * (an engine that reserved HBM for its KV cache up front, a foreign-language

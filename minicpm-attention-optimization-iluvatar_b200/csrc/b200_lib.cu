@@ -21,7 +21,6 @@
 
 #include "minicpm_b200.h"
 #include "paged_attention.cuh"
-#include "paged_attention_pair.cuh"
 #include "paged_decode.cuh"
 #include "rope_kv_cache.cuh"
 #include "split_combine.cuh"
@@ -150,12 +149,6 @@ bool decode_shape_ok(int group, int hkv) {
 bool use_decode_kernel() {
   const char* e = getenv("B200_ATTN_DECODE");
   return !(e && e[0] == '0');
-}
-
-// B200_ATTN_CTA_PAIR=1 selects the CTA-pair attention kernel, 0 the single-CTA one.
-bool use_cta_pair() {
-  const char* e = getenv("B200_ATTN_CTA_PAIR");
-  return e && e[0] == '1';
 }
 
 int auto_splits(int32_t total_q, int32_t num_seqs, int32_t hq, int32_t hkv, int32_t max_seqlen_k, int num_sms) {
@@ -296,6 +289,13 @@ int32_t b200_choose_num_splits(int32_t total_q, int32_t num_seqs, int32_t num_q_
   return auto_splits(total_q, num_seqs, num_q_heads, num_kv_heads, max_seqlen_k, sm_count());
 }
 
+int32_t b200_attn_shape_supported(int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t dtype) {
+  if (dtype != B200_DTYPE_BF16 && dtype != B200_DTYPE_F16) return 0;
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return 0;
+  if (num_q_heads / num_kv_heads > b200::kAttnTileM) return 0;
+  return head_dim == 64 || head_dim == b200::kAttnHeadDim;
+}
+
 size_t b200_attn_workspace_bytes(int32_t total_q, int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
                                  int32_t head_dim, int32_t num_splits, int32_t max_seqlen_k, int32_t dtype) {
   if (num_splits <= 0) num_splits = b200_choose_num_splits(total_q, num_seqs, num_q_heads, num_kv_heads, max_seqlen_k);
@@ -378,8 +378,8 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   if (p->head_dim != b200::kAttnHeadDim && p->head_dim != 64)
     return fail(B200_ERR_UNSUPPORTED, "head_dim %d: the sm_100a kernel handles head_dim 64 and 128", p->head_dim);
   const int group = p->num_q_heads / p->num_kv_heads;
-  if (group > b200::kAttnTileM || b200::kAttnTileM % group)
-    return fail(B200_ERR_UNSUPPORTED, "query heads per KV head (%d) must divide 128", group);
+  if (group > b200::kAttnTileM)
+    return fail(B200_ERR_UNSUPPORTED, "query heads per KV head (%d) must be at most 128", group);
   if (p->num_splits < 0 || p->num_splits > b200::kMaxSplits)
     return fail(B200_ERR_INVALID, "num_splits must be 0 (auto) or in [1, 16]");
   if (p->num_seqs < 0 || p->total_q < 0 || p->num_blocks <= 0 || p->block_table_cols <= 0)
@@ -433,11 +433,8 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   }
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // CTA-pair kernel (M = 256 UMMA across two SMs) or single-CTA kernel; the
-  // single-CTA kernel takes per-KV-head maps (4 KB boxes) when they fit.
-  // Per-KV-head maps and the CTA-pair kernel assume full 128-column rows.
-  const bool pair = use_cta_pair() && p->head_dim == b200::kAttnHeadDim;
-  const bool head_maps = !pair && p->num_kv_heads <= b200::kMaxHeadMaps && p->head_dim == b200::kAttnHeadDim;
+  // Per-KV-head maps (4 KB boxes) when they fit; they assume full 128-column rows.
+  const bool head_maps = p->num_kv_heads <= b200::kMaxHeadMaps && p->head_dim == b200::kAttnHeadDim;
   b200::KvHeadMaps maps;
   if (head_maps) {
     if (int r = encode_kv_head_maps(p, dt, &maps)) return r;
@@ -446,13 +443,12 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
     maps.k[0] = tm_k;
     maps.v[0] = tm_v;
   }
-  const int units_per_tile_group = pair ? b200::kPairTilesPerUnit : b200::kAttnTilesPerUnit;
   b200::SchedArgs sa{};
   sa.cu_q = p->cu_seqlens_q;
   sa.seqused = p->seqused_k;
   sa.len_i64 = p->seqlen_dtype == B200_DTYPE_I64;
   sa.num_seqs = p->num_seqs;
-  sa.pos_per_unit = ppt * units_per_tile_group;
+  sa.pos_per_unit = ppt * b200::kAttnTilesPerUnit;
   sa.num_kv_heads = p->num_kv_heads;
   sa.num_splits = splits;
   sa.capacity = w.capacity;
@@ -489,13 +485,11 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   a.head_dim = p->head_dim;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
-  // Upper bound on work units for this unit size (surplus CTAs of the pair
-  // kernel exit at once).
+  // Upper bound on work units; the kernel is persistent: one CTA per SM at most.
   const int64_t units_ub =
       ((int64_t)p->total_q + sa.pos_per_unit - 1) / sa.pos_per_unit + p->num_seqs;
-  const int64_t ctas = units_ub * p->num_kv_heads * splits * (pair ? 2 : 1);
-  // The single-CTA kernel is persistent: one CTA per SM at most.
-  const dim3 grid(static_cast<unsigned>(pair ? ctas : std::min<int64_t>(ctas, sm_count())));
+  const int64_t ctas = units_ub * p->num_kv_heads * splits;
+  const dim3 grid(static_cast<unsigned>(std::min<int64_t>(ctas, sm_count())));
   auto launch = [&](auto kernel, const auto&... args) -> int {
     // The kernel rebalances registers between warpgroups with setmaxnreg; the
     // split adds up only if every thread was launched with exactly
@@ -504,7 +498,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
     if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess || fa.numRegs != b200::kAttnLaunchRegs)
       return fail(B200_ERR_CUDA, "paged_attn_fwd_kernel built with %d registers per thread, %d expected", fa.numRegs,
                   b200::kAttnLaunchRegs);
-    const uint32_t smem = pair ? b200::kAttnPairSmemAlloc : b200::kAttnSmemAlloc;
+    const uint32_t smem = b200::kAttnSmemAlloc;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     // A programmatic dependent of the schedule kernel: launched while it runs,
     // it waits for it (griddepcontrol.wait) before reading the work list.
@@ -523,10 +517,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   };
   const bool bf16 = p->dtype == B200_DTYPE_BF16;
   int lr;
-  if (pair)
-    lr = bf16 ? launch(b200::paged_attn_fwd_pair_kernel<__nv_bfloat16>, tm_q, tm_k, tm_v, a)
-              : launch(b200::paged_attn_fwd_pair_kernel<__half>, tm_q, tm_k, tm_v, a);
-  else if (head_maps)
+  if (head_maps)
     lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, true>, tm_q, maps, a)
               : launch(b200::paged_attn_fwd_kernel<__half, true>, tm_q, maps, a);
   else

@@ -11,9 +11,10 @@
 //     and l, which b200_split_combine reduces.
 //
 // Work unit = (sequence, KV head, query-tile pair, split).  A query tile packs
-// the G = Hq / KH query heads that share one KV head with P = 128 / G query
-// positions into the 128 rows of one UMMA M dimension (row r = position
-// r / G, head r % G), so every K/V tile fetched feeds all G heads.  A unit
+// the G = Hq / KH query heads that share one KV head with P = floor(128 / G)
+// query positions into the rows of one 128-row UMMA M dimension (row r =
+// position r / G, head r % G; rows past G x P are zero padding when G does not
+// divide 128), so every K/V tile fetched feeds all G heads.  A unit
 // holds two such tiles (2P consecutive positions, 256 rows) that share every
 // K/V tile; the second is skipped when the sequence has no rows for it.
 //
@@ -123,8 +124,8 @@ struct AttnKernelArgs {
   int len_i64;
   int total_q;
   int num_q_heads;
-  int group;          // G = Hq / KH
-  int pos_per_tile;   // P = 128 / G
+  int group;          // G = Hq / KH, 1..128
+  int pos_per_tile;   // P = floor(128 / G)
   int block_size;
   int num_blocks;
   int num_splits;
@@ -259,6 +260,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_alloc(smem_addr(tmem_slot), kAttnTmemCols);
     tmem_relinquish();
   }
+  // A query tile holds G x P (position, head) rows; with G not dividing 128
+  // the last 128 - G x P rows are never loaded.  Zero them once so that their
+  // (unstored) S rows stay finite and every softmax warp keeps its fast path.
+  const int q_rows = a.group * P;
+  if (q_rows < kAttnTileM) {
+    const int pad = kAttnTileM - q_rows;
+    for (int i = threadIdx.x; i < 4 * pad * 8; i += kAttnThreads) {  // 2 tiles x 2 halves x pad rows x 8 pieces
+      const int r = q_rows + (i >> 3) % pad, part = (i >> 3) / pad;
+      st_shared_v4(sbase + kSmQ + part * 16384 + r * 128 + (i & 7) * 16, 0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -338,7 +351,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (ok) {
             const int head0 = e.kvh * a.group;
             const int t0 = ug.q_begin + ug.pos0;
-            mbar_arrive_expect_tx(bar(BAR_Q_FULL), (two ? 2 : 1) * 32768);
+            mbar_arrive_expect_tx(bar(BAR_Q_FULL), (two ? 2 : 1) * q_rows * 256);  // 2 halves of 128 B rows
             tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q_FULL), 0, head0, t0);
             tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q_FULL), 64, head0, t0);
             if (two) {
@@ -538,7 +551,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int tile_pos0 = ug.pos0 + t * P;
       const int row_pos = tile_pos0 + row / a.group;
       const int row_head = e.kvh * a.group + row % a.group;
-      const bool row_valid = row_pos < ug.q_len;
+      const bool row_valid = row < q_rows && row_pos < ug.q_len;
       const int q_abs = ug.q_abs_min + t * P + row / a.group;
       const int row_hi = min(ug.split_end, q_abs + 1);
       const int unmasked_hi = min(ug.split_end, ug.q_abs_min + t * P + 1);

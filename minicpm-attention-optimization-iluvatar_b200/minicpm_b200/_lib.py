@@ -61,6 +61,7 @@ EXPORTED_SYMBOLS = (
     "b200_last_error",
     "b200_choose_num_splits",
     "b200_attn_workspace_bytes",
+    "b200_attn_shape_supported",
     "b200_paged_attn_fwd",
     "b200_split_combine",
     "b200_paged_attn_fwd_noalloc",
@@ -161,6 +162,8 @@ def load() -> ctypes.CDLL:
         lib.b200_choose_num_splits.argtypes = [i32] * 5
         lib.b200_attn_workspace_bytes.restype = ctypes.c_size_t
         lib.b200_attn_workspace_bytes.argtypes = [i32] * 8
+        lib.b200_attn_shape_supported.restype = i32
+        lib.b200_attn_shape_supported.argtypes = [i32] * 4
         lib.b200_paged_attn_fwd.restype = ctypes.c_int
         lib.b200_paged_attn_fwd.argtypes = [ctypes.POINTER(AttnParams), c_void_p]
         lib.b200_split_combine.restype = ctypes.c_int

@@ -10,6 +10,10 @@ same signature, same feature guards, same routing, same exceptions.
   (``max_seqlen_q <= 1``, softcap, KV quantisation, ALiBi, a sliding
   window, ``q_descale``, sinks, ``use_td``); failures on that path propagate,
   there is no silent fallback (``kernels/attention.py:151-152``).
+* A head shape or element type the sm_100a kernel does not run (fp32,
+  head_dim 256, more than 128 query heads per KV head; ``kernel_supports``)
+  is routed like an unsupported feature: the reference's Triton kernel took
+  these shapes, so they must not turn into an error here.
 * Otherwise the call goes to vLLM's ``unified_attention``, as in the
   reference, and ``RuntimeError`` is raised when vLLM is not importable
   (``kernels/attention.py:112-117``).  That route is vLLM's own kernel and is
@@ -33,6 +37,7 @@ from typing import Optional
 
 import torch
 
+from .split_kv_paged import kernel_supports
 from .unified_attention_optimized import unified_attention_optimized
 
 
@@ -122,6 +127,7 @@ def iluvatar_attention(
         or q_descale is not None
         or sinks is not None
         or use_td
+        or not kernel_supports(q, k)
     )
 
     if use_baseline:

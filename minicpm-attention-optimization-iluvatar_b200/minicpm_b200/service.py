@@ -8,7 +8,9 @@ reference's integration patch adds it (``integration/vllm-plugin-FL-split-kv.pat
   ``ILUVATAR_SPLIT_KV`` are both set ("1", "true" or "yes") and the call uses
   no unsupported feature (KV quantisation, ALiBi, sinks, softcap, a sliding
   window, any descale, tensor descriptors, non-causal), else vLLM's
-  ``unified_attention``.  Pure decode (``max_seqlen_q <= 1``) stays on vLLM
+  ``unified_attention``.  A head shape or dtype the sm_100a kernel does not
+  run (``kernel_supports``: fp32, head_dim 256, more than 128 query heads per
+  KV head) takes the vLLM route too.  Pure decode (``max_seqlen_q <= 1``) stays on vLLM
   unless ``ILUVATAR_SPLIT_KV_DECODE`` is also set, which selects the sm_100a
   decode kernel (the reference kept decode on vLLM).  Failures of the sm_100a
   path propagate; there is no silent fallback.
@@ -57,6 +59,7 @@ from .kv_cache import (
     reshape_and_cache_flash_per_token_head_quant,
     rope_and_cache,
 )
+from .split_kv_paged import kernel_supports
 from .unified_attention_optimized import unified_attention_optimized
 
 
@@ -125,6 +128,7 @@ def _run_unified_attention(**kwargs: Any) -> torch.Tensor:
         or kwargs.get("v_descale") is not None
         or kwargs.get("use_td", False)
         or kwargs.get("causal") is not True
+        or not kernel_supports(kwargs["q"], kwargs["k"])
     )
     decode_only = max_query_len <= 1
     if not enabled or unsupported or max_query_len < 1 or (decode_only and not _flag("ILUVATAR_SPLIT_KV_DECODE")):

@@ -151,9 +151,27 @@ def split_kv_combine(o_splits: torch.Tensor, m_splits: torch.Tensor, l_splits: t
     return out
 
 
+def kernel_supports(q: torch.Tensor, k: torch.Tensor) -> bool:
+    """Whether the sm_100a kernel runs this call's head shape and element type.
+
+    ``q`` is ``[T, Hq, D]``; ``k`` is the 4-D ``[blocks, block, KH, D]`` cache
+    or the 5-D ``[blocks, 2, block, KH, D]`` one.  The dispatcher and the
+    service route calls for which this is false (fp32, head_dim 256, more than
+    128 query heads per KV head) to their baseline kernel, as they route the
+    features the kernel does not implement.
+    """
+    try:
+        code = _lib.dtype_code(q.dtype)
+    except ValueError:
+        return False
+    if q.ndim != 3 or k.ndim not in (4, 5) or k.dtype != q.dtype:
+        return False
+    return bool(_lib.load().b200_attn_shape_supported(int(q.shape[1]), int(k.shape[-2]), int(q.shape[2]), code))
+
+
 def choose_num_splits(total_q: int, num_seqs: int, num_q_heads: int, num_kv_heads: int, max_seqlen_k: int) -> int:
     """The split count ``num_splits=0`` resolves to on the current device."""
     return int(_lib.load().b200_choose_num_splits(total_q, num_seqs, num_q_heads, num_kv_heads, max_seqlen_k))
 
 
-__all__ = ["paged_split_kv_attention", "split_kv_combine", "choose_num_splits"]
+__all__ = ["paged_split_kv_attention", "split_kv_combine", "choose_num_splits", "kernel_supports"]

@@ -19,7 +19,7 @@ recorded here, so a changed generator fails loudly instead of silently.
 
 Usage (only where the reference project is mounted)::
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <checkout of the reference project>
 """
 
 from __future__ import annotations
@@ -169,9 +169,12 @@ def rope_case(is_neox: bool, rotary_dim: int):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("MINICPM_REFERENCE_DIR"),
+                    help="checkout of the reference project (or set MINICPM_REFERENCE_DIR)")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or MINICPM_REFERENCE_DIR) must name the reference project's checkout")
     sys.path.insert(0, args.reference)
     torch.set_num_threads(os.cpu_count() or 1)
     for case in ATTN_CASES:

@@ -216,6 +216,20 @@ def test_dispatcher_unsupported_features_go_to_vllm(routes, monkeypatch, over):
     assert len(baseline.calls) == 1 and not optimized.calls
 
 
+@pytest.mark.parametrize("hq,hkv,d,dtype,optimized_route", [
+    (16, 2, 256, torch.bfloat16, False), (16, 2, 128, torch.float32, False), (256, 1, 128, torch.bfloat16, False),
+    (12, 2, 128, torch.bfloat16, True), (16, 2, 64, torch.float16, True)])
+def test_dispatcher_routes_shapes_the_kernel_does_not_run_to_vllm(routes, monkeypatch, hq, hkv, d, dtype,
+                                                                  optimized_route):
+    baseline, optimized = routes
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    q = torch.empty(8, hq, d, dtype=dtype, device="meta")
+    cache = torch.empty(4, 2, 16, hkv, d, dtype=dtype, device="meta")
+    minicpm_b200.iluvatar_attention(**_dispatch_args(q=q, k=cache, v=cache, out=q))
+    assert (len(optimized.calls), len(baseline.calls)) == ((1, 0) if optimized_route else (0, 1))
+
+
 def test_dispatcher_optimized_route_and_5d_unbind(routes, monkeypatch):
     baseline, optimized = routes
     monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")

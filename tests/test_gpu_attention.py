@@ -109,8 +109,10 @@ def test_fp16():
     assert_close(got, oracle(batch), "fp16")
 
 
-@pytest.mark.parametrize("hq,hkv", [(8, 1), (16, 16), (32, 2), (4, 2)])
+@pytest.mark.parametrize("hq,hkv", [(8, 1), (16, 16), (32, 2), (4, 2), (12, 2), (6, 2), (40, 4), (80, 1), (128, 1)])
 def test_other_gqa_ratios(hq, hkv):
+    """Ratios that divide 128 and ratios that do not (6:1, 3:1, 10:1, 80:1: a
+    query tile holds floor(128 / G) positions x G heads, the rest is padding)."""
     batch = small_batch([19, 70], [45, 300], seed=13, num_q_heads=hq, num_kv_heads=hkv)
     for s in (1, 4):
         assert_close(run_gpu(batch, s), oracle(batch), f"gqa {hq}/{hkv} S={s}")

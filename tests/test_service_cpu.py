@@ -25,8 +25,16 @@ def routes(monkeypatch):
     return calls
 
 
+def _qk(hq=16, hkv=2, d=128, dtype=torch.bfloat16):
+    """Shape-only tensors (meta device: no storage) for the route's shape check."""
+    q = torch.empty(64, hq, d, dtype=dtype, device="meta")
+    k = torch.empty(8, 16, hkv, d, dtype=dtype, device="meta")
+    return q, k
+
+
 def _kwargs(**over):
-    kw = dict(q=None, k=None, v=None, out=None, cu_seqlens_q=None, max_seqlen_q=64, seqused_k=None, max_seqlen_k=100,
+    q, k = _qk()
+    kw = dict(q=q, k=k, v=k, out=q, cu_seqlens_q=None, max_seqlen_q=64, seqused_k=None, max_seqlen_k=100,
               softmax_scale=0.1, causal=True, block_table=None, alibi_slopes=None, window_size=(-1, -1), softcap=0.0,
               q_descale=None, k_descale=None, v_descale=None, sinks=None, kv_quant_mode=service.KVQuantMode.NONE,
               use_td=False)
@@ -73,6 +81,25 @@ def test_unsupported_features_and_decode_stay_on_vllm(routes, monkeypatch, over)
     monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
     service._run_unified_attention(**_kwargs(**over))
     assert routes[-1][0] == "vllm"
+
+
+@pytest.mark.parametrize(
+    "shape,route",
+    [
+        (dict(d=256), "vllm"),  # head_dim 256: the reference's Triton kernel took it, the sm_100a kernel does not
+        (dict(hq=12, hkv=2), "b200"),  # GQA 6:1 (128 rows hold 21 positions x 6 heads)
+        (dict(hq=24, hkv=2), "b200"),  # GQA 12:1
+        (dict(hq=256, hkv=1), "vllm"),  # more than 128 query heads per KV head
+        (dict(dtype=torch.float32), "vllm"),
+        (dict(d=64), "b200"),
+    ],
+)
+def test_shapes_the_kernel_does_not_run_go_to_vllm(routes, monkeypatch, shape, route):
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    q, k = _qk(**shape)
+    service._run_unified_attention(**_kwargs(q=q, k=k, v=k, out=q))
+    assert routes[-1][0] == route
 
 
 def test_decode_flag_routes_decode_to_b200(routes, monkeypatch):

@@ -6,9 +6,13 @@
 Default workload: chunked prefill at 16K context -- 64 sequences, 2048-token
 query chunks, total KV length uniform in [8192, 16384], 16 query heads / 2 KV
 heads, head_dim 128, bf16, page size 16, permuted block table.  Under
-torchrun the sequences are sharded contiguously over the ranks (one process
-per GPU, no collective in the timed region); the reported value is the
-causal FLOPs of all ranks divided by the slowest rank's device time.
+torchrun the sequences are sharded over the ranks by causal FLOPs
+(longest-processing-time first; one process per GPU, no collective in the
+timed region); the reported value is the causal FLOPs of all ranks divided by
+the slowest rank's device time.  The line's ``sub`` object carries the rest of
+the metric from the same run: the 4K config at S = auto / 4 / 8, the mixed
+256-sequence batch, the RoPE + KV-cache write at rotary_dim 64 / 128 x NeoX /
+interleaved and the Split-KV combine, each with its roofline fraction.
 
 One JSON line on rank 0.  ``value``: device-resident throughput (inputs in HBM
 before the timed region).  ``e2e``: the same metric through the public
@@ -68,6 +72,8 @@ def parse_args():
     ap.add_argument("--graph", action="store_true",
                     help="attention workloads: time the K calls as one CUDA graph replay (no host launch gaps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="16K workload: skip the 4K / mixed / RoPE / combine entries of the line's \"sub\" object")
     ap.add_argument("--verify", action="store_true", help="gather outputs to rank 0 (NCCL) and check sampled rows")
     return ap.parse_args()
 
@@ -195,23 +201,17 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- workloads
-def shard(n: int, world: int, rank: int) -> list[int]:
-    from minicpm_b200.sharding import contiguous_shard
-
-    return contiguous_shard(n, world, rank)
-
-
 def build_local_batch(workload: str, world: int, rank: int, num_seqs: int = 0):
+    """This rank's sequences: longest-processing-time assignment by causal FLOPs
+    (the KV lengths of one batch vary 2x to 30x, so equal counts leave the
+    slowest rank well behind the mean)."""
     from minicpm_b200 import workloads
     from minicpm_b200.sharding import lpt_shard
 
     q, kv = workloads.WORKLOADS[workload]()
     if num_seqs:
         q, kv = q[:num_seqs], kv[:num_seqs]
-    if workload == "mixed_256":
-        ids = lpt_shard(q, kv, world, 16, 128)[rank]
-    else:
-        ids = shard(len(q), world, rank)
+    ids = lpt_shard(q, kv, world, 16, 128)[rank]
     batch = workloads.build_attention_batch([q[i] for i in ids], [kv[i] for i in ids], seq_ids=ids)
     return batch, q, kv
 
@@ -248,14 +248,54 @@ def time_cpu(run, reps: int):
     return times
 
 
+# --------------------------------------------------------------------- shared config
+def attention_config(workload: str, world: int, splits: int, num_seqs: int = 0) -> dict:
+    """The workload's ``config`` object, identical in both arms: the shapes and
+    FLOPs of the whole job (all ranks), the split count the call resolves
+    (``splits`` 0 = automatic), the sharding and the L2 note."""
+    from minicpm_b200 import workloads
+    from minicpm_b200.split_kv_paged import choose_num_splits
+    from oracle import causal_flops  # FLOP formula of the reference harness (no compute)
+
+    q, kv = workloads.WORKLOADS[workload]()
+    if num_seqs:
+        q, kv = q[:num_seqs], kv[:num_seqs]
+    if splits:
+        resolved = splits
+    else:
+        from minicpm_b200.sharding import lpt_shard
+
+        # rank 0's shard decides the automatic count the call resolves to
+        ids = lpt_shard(q, kv, world, 16, 128)[0]
+        resolved = choose_num_splits(sum(q[i] for i in ids), len(ids), 16, 2, max(kv[i] for i in ids))
+    kv_mb = sum(workloads.attention_kv_bytes([0], [L]) for L in kv) / 1e6 / world
+    q_mb = sum(q) * 16 * 128 * 2 / 1e6 / world
+    return {
+        "workload": workload,
+        "seqs": len(q),
+        "query_tokens": sum(q),
+        "causal_flops": float(causal_flops(q, kv, 16, 128)),
+        "heads": "16q/2kv", "head_dim": 128, "page_size": 16,
+        "num_splits": resolved,
+        "parallelism": f"sequence-sharded x{world} (LPT by causal FLOPs)",
+        "l2": "inputs larger than L2 (KV %.0f MB + Q %.0f MB per GPU)" % (kv_mb, q_mb),
+    }
+
+
 # --------------------------------------------------------------------- reference arm
 def reference_arm(args, world, rank):
-    """The CPU implementation of the path (the fp32 oracle port), timed on host cores."""
+    """The CPU implementation of the path (the fp32 oracle port), timed on host cores.
+
+    Each step runs the oracle over a bounded sample of the workload (the last
+    512 query rows of its first sequence, full causal KV context) and the rate
+    is reported in the workload's own unit; ``config`` is the same object the
+    sm_100a arm prints.
+    """
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    if args.workload == "rope_16384":
-        print(json.dumps({"impl": "reference", "unavailable": "reference arm covers the attention workloads"}))
+    if args.workload not in ("chunked_prefill_16k", "chunked_prefill_4k", "mixed_256"):
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm covers the prefill attention workloads"}))
         return
     from minicpm_b200 import workloads
 
@@ -270,9 +310,9 @@ def reference_arm(args, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak" if args.workload == "mixed_256" else "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "sample": desc},
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) q/k/v, random-permuted page table)",
+        "config": attention_config(args.workload, world, args.splits, args.num_seqs),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -281,21 +321,26 @@ def reference_arm(args, world, rank):
 
 
 # --------------------------------------------------------------------- RoPE bench
-def rope_bench(args, world, rank, local):
-    """RoPE + paged KV-cache write of 16384 tokens (the reference operator, or with
-    ``--service`` the service's call: key rotated in place, ``--kv-dtype fp8`` caches)."""
+def rope_run(rotary_dim: int, is_neox: bool, service: bool, kv_dtype: str, steps: int, warmup: int, local: int,
+             world: int, clocks: bool = True) -> dict:
+    """Graph-timed RoPE + paged KV-cache write of 16384 tokens on this GPU.
+
+    The reference operator, or with ``service`` the service's call (key rotated
+    in place; ``kv_dtype`` "fp8" caches).  Returns GB/s of this GPU, the device
+    time per launch, the algorithmic bytes and the clock record.
+    """
     from minicpm_b200 import fused_rope_and_cache, kv_cache
     from minicpm_b200.workloads import build_rope_batch, rope_algorithmic_bytes
 
     dev = torch.device("cuda", local)
-    b = build_rope_batch(16384, rotary_dim=args.rotary_dim, is_neox=not args.interleaved)
+    b = build_rope_batch(16384, rotary_dim=rotary_dim, is_neox=is_neox)
     g = b.to(dev)
     nbytes = rope_algorithmic_bytes(b)
-    fp8 = args.service and args.kv_dtype == "fp8"
-    if args.service:
+    fp8 = service and kv_dtype == "fp8"
+    if service:
         t, hkv, d = b.key.shape
         written = int((b.slot_mapping >= 0).sum())
-        nbytes += 2 * t * hkv * args.rotary_dim * b.key.element_size()  # rotated key written back
+        nbytes += 2 * t * hkv * rotary_dim * b.key.element_size()  # rotated key written back
         if fp8:
             nbytes -= 2 * written * hkv * d * (b.key.element_size() - 1)  # 1-byte cache rows
             g.key_cache = torch.zeros(g.key_cache.shape, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
@@ -303,37 +348,44 @@ def rope_bench(args, world, rank, local):
         ks = torch.tensor([0.02], device=dev)
         vs = torch.tensor([0.015], device=dev)
 
-    def step():
-        if args.service:
+    def step(i):
+        if service:
             kv_cache.rope_and_cache(g.query, g.key, g.value, g.positions, g.cos_sin_cache, g.is_neox, g.key_cache,
                                     g.value_cache, g.slot_mapping, ks, vs, True, fp8)
         else:
             fused_rope_and_cache(g.query, g.key, g.value, g.positions, g.cos_sin_cache, g.is_neox, g.key_cache,
                                  g.value_cache, g.slot_mapping)
 
-    for _ in range(args.warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     # Back-to-back launches replayed from a CUDA graph: the ~170 MB one launch
     # moves exceed the 126 MB L2, so each launch streams from HBM.
-    ms, clocks = graph_timed(lambda i: step(), args.steps, local, world)
+    ms, clk = graph_timed(step, steps, local, world, clocks=clocks)
+    return {"gbs": nbytes / (ms * 1e-3) / 1e9, "ms": ms, "nbytes": nbytes, "clocks": clk, "batch": b, "fp8": fp8}
+
+
+def rope_bench(args, world, rank, local):
+    """RoPE + paged KV-cache write of 16384 tokens (the reference operator, or with
+    ``--service`` the service's call: key rotated in place, ``--kv-dtype fp8`` caches)."""
+    r = rope_run(args.rotary_dim, not args.interleaved, args.service, args.kv_dtype, args.steps, args.warmup, local,
+                 world)
     peaks, kind = measured_peaks()
-    gbs = nbytes / (ms * 1e-3) / 1e9
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
-        cpu = rope_cpu_baseline(b, nbytes)
+        cpu = rope_cpu_baseline(r["batch"], r["nbytes"])
     if rank == 0:
         line = {
-            "metric": "RoPE + paged KV-cache write GB/s", "value": gbs * world, "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "metric": "RoPE + paged KV-cache write GB/s", "value": r["gbs"] * world, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "rope_16384", "tokens": 16384, "rotary_dim": args.rotary_dim,
                        "is_neox": not args.interleaved, "service": bool(args.service),
-                       "cache": "fp8_e4m3" if fp8 else "bf16", "algorithmic_bytes": nbytes,
+                       "cache": "fp8_e4m3" if r["fp8"] else "bf16", "algorithmic_bytes": r["nbytes"],
                        "l2": "inputs larger than L2, back-to-back launches",
                        "timing": "CUDA graph of all timed launches, replayed once"},
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": kind},
-            "clocks": clocks,
+            "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": r["gbs"] / peaks["hbm_gbs"], "traffic": None, "peak_kind": kind},
+            "clocks": r["clocks"],
             "gpu_launches": args.steps,
         }
         if cpu:
@@ -360,7 +412,7 @@ def rope_cpu_baseline(b, nbytes):
 
 
 # --------------------------------------------------------------------- graph-timed short kernels
-def graph_timed(step, steps: int, local: int, world: int):
+def graph_timed(step, steps: int, local: int, world: int, clocks: bool = True):
     """Device time per launch of ``step(i)``, i = 0..steps-1, captured in one CUDA graph.
 
     Kernels of a few to tens of microseconds launched one by one from Python
@@ -380,14 +432,20 @@ def graph_timed(step, steps: int, local: int, world: int):
     torch.cuda.synchronize(local)
     barrier(world)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    sampler = ClockSampler(local) if clocks else None
+    if sampler:
+        sampler.__enter__()
+    try:
         s.record()
         graph.replay()
         e.record()
         e.synchronize()
+    finally:
+        if sampler:
+            sampler.__exit__(None, None, None)
     ms = max_over_ranks(s.elapsed_time(e) / steps, world)
     del graph
-    return ms, clocks.summary()
+    return ms, (sampler.summary() if sampler else None)
 
 
 # --------------------------------------------------------------------- KV-cache write bench
@@ -477,18 +535,17 @@ def kv_write_cpu_baseline(b, nbytes):
 
 
 # --------------------------------------------------------------------- split-combine bench
-def combine_bench(args, world, rank, local):
-    """The cross-split reduce on the partials of the 4K chunked-prefill batch.
+def combine_run(s_count: int, steps: int, warmup: int, local: int, world: int, clocks: bool = True) -> dict:
+    """Graph-timed cross-split reduce on the partials of the 4K chunked-prefill batch.
 
-    32768 query tokens x 16 heads x 128, ``--splits`` partials (default 4) in
-    bf16 with fp32 m/l, every split holding keys (l > 0), so every partial is
-    read: algorithmic bytes = S*T*H*(D*2 + 8) read + T*H*D*2 written (688 MB
-    at S = 4, larger than L2).
+    32768 query tokens x 16 heads x 128, ``s_count`` partials in bf16 with fp32
+    m/l, every split holding keys (l > 0), so every partial is read:
+    algorithmic bytes = S*T*H*(D*2 + 8) read + T*H*D*2 written (688 MB at
+    S = 4, larger than L2).
     """
     from minicpm_b200 import split_kv_combine
 
     dev = torch.device("cuda", local)
-    s_count = args.splits if args.splits > 1 else 4
     t, h, d = 32768, 16, 128
     gen = torch.Generator().manual_seed(20260928)
     o = torch.randn(s_count, t, h, d, generator=gen).to(torch.bfloat16).to(dev)
@@ -500,36 +557,44 @@ def combine_bench(args, world, rank, local):
     def step(i):
         split_kv_combine(o, m, l, out)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step(0)
-    ms, clocks = graph_timed(step, args.steps, local, world)
+    ms, clk = graph_timed(step, steps, local, world, clocks=clocks)
+    return {"gbs": nbytes / (ms * 1e-3) / 1e9, "ms": ms, "nbytes": nbytes, "clocks": clk, "o": o, "m": m, "l": l,
+            "out": out, "shape": (t, h, d)}
+
+
+def combine_bench(args, world, rank, local):
+    """The Split-KV combine alone (``--splits`` partials, default 4) on 4K-batch-sized partials."""
+    s_count = args.splits if args.splits > 1 else 4
+    r = combine_run(s_count, args.steps, args.warmup, local, world)
     peaks, pkind = measured_peaks()
-    gbs = nbytes / (ms * 1e-3) / 1e9
+    t, h, d = r["shape"]
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         from oracle import split_kv_reduce_reference
 
         torch.set_num_threads(os.cpu_count() or 1)
         n = 2048
-        oc, mc, lc = o[:, :n].float().cpu(), m[:, :n].cpu(), l[:, :n].cpu()
+        oc, mc, lc = r["o"][:, :n].float().cpu(), r["m"][:, :n].cpu(), r["l"][:, :n].cpu()
         want = split_kv_reduce_reference(oc, mc, lc)
-        got = out[:n].float().cpu()
+        got = r["out"][:n].float().cpu()
         assert (got - want).abs().max().item() <= 2e-2, "combine differs from the oracle"
         times = time_cpu(lambda: split_kv_reduce_reference(oc, mc, lc), 3)
-        cpu = {"value": nbytes * n / t / (sum(times) / len(times)) / 1e9, "unit": "GB/s",
+        cpu = {"value": r["nbytes"] * n / t / (sum(times) / len(times)) / 1e9, "unit": "GB/s",
                "cores": torch.get_num_threads(), "kind": "port",
                "sample": f"first {n} of {t} tokens, 3 repetitions (bytes scaled to the sample)"}
     if rank == 0:
         line = {
-            "metric": "Split-KV combine GB/s", "value": gbs * world, "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "metric": "Split-KV combine GB/s", "value": r["gbs"] * world, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "split_combine_4k", "tokens": t, "heads": h, "head_dim": d, "splits": s_count,
-                       "algorithmic_bytes": nbytes, "l2": "inputs larger than L2, back-to-back launches",
+                       "algorithmic_bytes": r["nbytes"], "l2": "inputs larger than L2, back-to-back launches",
                        "timing": "CUDA graph of all timed launches, replayed once"},
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": pkind},
-            "clocks": clocks,
+            "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": r["gbs"] / peaks["hbm_gbs"], "traffic": None, "peak_kind": pkind},
+            "clocks": r["clocks"],
             "gpu_launches": args.steps,
         }
         if cpu:
@@ -573,7 +638,8 @@ def verify_sharded(args, batch, out, world, rank, splits):
 
 # --------------------------------------------------------------------- e2e (host buffers)
 E2E_MAX_GROUPS = 8
-E2E_MIN_SEQS_PER_GROUP = 4
+E2E_MIN_SEQS_PER_GROUP = 4   # with more than 16 sequences on the rank
+E2E_MIN_GROUPS = 4           # fewer sequences: groups of one or two, so several groups are in flight
 
 
 def split_into_groups(batch, n_groups: int):
@@ -621,7 +687,9 @@ def e2e_pipelined(args, batch, out, splits, stream, world, total_flops, total_to
 
     Each step copies every input from pinned host memory and reads ``out``
     back, inside the timed region.  The batch's sequences go in up to eight
-    groups (at least four sequences each), each with its own page pool: group
+    groups (at least four sequences each when the rank holds more than 16, else
+    groups of one or two so that at least four are in flight), each with its
+    own page pool: group
     i's host-to-device copies (one stream) overlap group i-1's attention call
     (torch's current stream) and group i-2's read-back (a third stream), so
     the step costs about the PCIe time of its bytes rather than the sum of
@@ -636,7 +704,11 @@ def e2e_pipelined(args, batch, out, splits, stream, world, total_flops, total_to
         os.environ["ILUVATAR_NUM_SPLITS"] = str(splits)
     dev = out.device
     nseq = len(batch.query_lens)
-    n_groups = max(1, min(E2E_MAX_GROUPS, nseq // E2E_MIN_SEQS_PER_GROUP))
+    if nseq > 4 * E2E_MIN_SEQS_PER_GROUP:
+        n_groups = min(E2E_MAX_GROUPS, nseq // E2E_MIN_SEQS_PER_GROUP)
+    else:
+        n_groups = min(nseq, max(E2E_MIN_GROUPS, nseq // 2), E2E_MAX_GROUPS)
+    n_groups = max(1, n_groups)
     parts = split_into_groups(batch, n_groups)
     keys = ("q", "kv_cache", "block_table", "cu_seqlens_q", "seqused_k")
     host = [{k: getattr(p, k).pin_memory() for k in keys} for p in parts]
@@ -704,56 +776,61 @@ def e2e_pipelined(args, batch, out, splits, stream, world, total_flops, total_to
 
 
 # --------------------------------------------------------------------- attention bench
-def attention_bench(args, world, rank, local):
-    from minicpm_b200 import iluvatar_attention, paged_split_kv_attention
+def attention_run(workload: str, splits: int, steps: int, warmup: int, world: int, rank: int, local: int,
+                  num_seqs: int = 0, graph: bool = False, clocks: bool = True) -> dict:
+    """Device-resident timing of ``steps`` back-to-back calls on this rank's shard.
+
+    Barrier + synchronize on both sides of the timed region, CUDA events on the
+    launching stream, the slowest rank's time.  Returns the whole-job figures
+    and this rank's per-launch times.
+    """
+    from minicpm_b200 import paged_split_kv_attention
     from minicpm_b200.split_kv_paged import choose_num_splits
+    from minicpm_b200.workloads import attention_kv_bytes
     from oracle import causal_flops  # FLOP formula of the reference harness (no compute)
 
-    from minicpm_b200.workloads import attention_kv_bytes
-
     dev = torch.device("cuda", local)
-    decode = args.workload.startswith("decode")
-    batch, all_q, all_kv = build_local_batch(args.workload, world, rank, args.num_seqs)
+    batch, all_q, all_kv = build_local_batch(workload, world, rank, num_seqs)
     local_flops = causal_flops(batch.query_lens, batch.kv_lens, 16, 128)
     local_bytes = attention_kv_bytes(batch.query_lens, batch.kv_lens)
-    total_bytes = sum_over_ranks(float(local_bytes), world) if world > 1 else float(local_bytes)
-    total_flops = sum_over_ranks(float(local_flops), world) if world > 1 else float(local_flops)
-    total_tokens = sum(all_q)
+    total_bytes = sum_over_ranks(float(local_bytes), world)
+    total_flops = sum_over_ranks(float(local_flops), world)
     g = batch.to(dev)
     out = torch.empty_like(g.q)
-    splits = args.splits
     resolved = splits or choose_num_splits(g.total_q, len(batch.query_lens), 16, 2, batch.max_seqlen_k)
 
     def step():
         paged_split_kv_attention(g.q, g.kv_cache[:, 0], g.kv_cache[:, 1], out, g.block_table, g.seqused_k,
                                  g.cu_seqlens_q, g.max_seqlen_q, g.max_seqlen_k, g.softmax_scale, num_splits=splits)
 
-    for _ in range(max(args.warmup, 1)):
+    for _ in range(max(warmup, 1)):
         step()
     barrier(world)
     stream = torch.cuda.current_stream(dev)
-    per_launch = []
-    if args.graph:
+    if graph:
         # The K calls captured in one CUDA graph (as a serving engine replays
         # its decode steps) and replayed once inside the events.
         gstream = torch.cuda.Stream(device=dev)
         gstream.wait_stream(stream)
-        graph = torch.cuda.CUDAGraph()
+        cuda_graph = torch.cuda.CUDAGraph()
         with torch.cuda.stream(gstream):
-            with torch.cuda.graph(graph, stream=gstream):
-                for _ in range(args.steps):
+            with torch.cuda.graph(cuda_graph, stream=gstream):
+                for _ in range(steps):
                     step()
         stream.wait_stream(gstream)
-        graph.replay()
+        cuda_graph.replay()
         torch.cuda.synchronize(dev)
         barrier(world)
-    with ClockSampler(dev.index) as clocks:
+    sampler = ClockSampler(dev.index) if clocks else None
+    if sampler:
+        sampler.__enter__()
+    try:
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         start.record(stream)
-        if args.graph:
-            graph.replay()
+        if graph:
+            cuda_graph.replay()
         else:
             for s, e in evs:
                 s.record(stream)
@@ -761,37 +838,130 @@ def attention_bench(args, world, rank, local):
                 e.record(stream)
         end.record(stream)
         end.synchronize()
+    finally:
+        if sampler:
+            sampler.__exit__(None, None, None)
     barrier(world)
     elapsed_ms = start.elapsed_time(end)
-    if args.graph:
-        per_launch = [elapsed_ms / args.steps] * args.steps
-        del graph
+    if graph:
+        per_launch = [elapsed_ms / steps] * steps
+        del cuda_graph
     else:
         per_launch = [s.elapsed_time(e) for s, e in evs]
     max_ms = max_over_ranks(elapsed_ms, world)
-    value = total_flops * args.steps / (max_ms * 1e-3) / 1e12
-    tokens_per_s = total_tokens * args.steps / (max_ms * 1e-3)
+    return {
+        "batch": batch, "g": g, "out": out, "stream": stream, "resolved": resolved,
+        "local_flops": local_flops, "local_bytes": local_bytes, "total_flops": total_flops,
+        "total_bytes": total_bytes, "total_tokens": sum(all_q), "all_q": all_q,
+        "max_ms": max_ms, "per_launch": per_launch, "launch_ms": statistics.mean(per_launch),
+        "value": total_flops * steps / (max_ms * 1e-3) / 1e12,
+        "tokens_per_s": sum(all_q) * steps / (max_ms * 1e-3),
+        "clocks": sampler.summary() if sampler else None,
+    }
+
+
+def traffic_per_launch(workload: str):
+    """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
+    tfile = ROOT / "profiles" / f"paged_attn_fwd_{workload}.traffic.json"
+    if tfile.exists():
+        try:
+            return json.loads(tfile.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+def sub_benchmarks(args, world, rank, local) -> dict:
+    """The rest of the metric, measured in the same run as the headline.
+
+    * the 4K chunked-prefill config at S = auto / 4 / 8 (TFLOP/s, sharded like
+      the headline);
+    * the mixed 256-sequence batch (half decode rows), LPT-sharded over the
+      ranks (TFLOP/s);
+    * the RoPE + KV-cache write at rotary_dim 64 / 128 x NeoX / interleaved
+      and the Split-KV combine at S = 4 (GB/s per GPU; every rank runs its own
+      replica, the value is the sum over ranks).
+
+    Each entry carries its roofline fraction against the measured peaks.
+    """
+    peaks, kind = measured_peaks()
+    steps, warmup = max(5, args.steps // 2), 3
+    subs = {}
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    try:
+        for workload, splits in (("chunked_prefill_4k", 0), ("chunked_prefill_4k", 4), ("chunked_prefill_4k", 8),
+                                 ("mixed_256", 0)):
+            r = attention_run(workload, splits, steps, warmup, world, rank, local, clocks=False)
+            achieved = r["local_flops"] / (r["launch_ms"] * 1e-3) / 1e12
+            name = f"{workload}_S{splits}" if splits else f"{workload}_auto"
+            subs[name] = {
+                "value": r["value"], "unit": "TFLOP/s", "ms_per_step": r["max_ms"] / steps, "steps": steps,
+                "gpu_launches": steps * (2 + (1 if r["resolved"] > 1 else 0)),
+                "tokens_per_s": r["tokens_per_s"], "num_splits": r["resolved"], "causal_flops": r["total_flops"],
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": achieved / peaks["bf16_tflops"],
+                             "traffic": traffic_per_launch(workload) if splits == 0 else None,
+                             "peak_kind": f"bf16_tflops (burst) of {kind}", "per_launch_ms": r["launch_ms"]},
+            }
+            del r
+            torch.cuda.empty_cache()
+        for rd in (64, 128):
+            for neox in (True, False):
+                n = max(10, args.steps)
+                r = rope_run(rd, neox, False, "auto", n, warmup, local, world, clocks=False)
+                subs[f"rope_16384_rd{rd}_{'neox' if neox else 'interleaved'}"] = {
+                    "value": r["gbs"] * world, "unit": "GB/s", "us_per_launch": r["ms"] * 1e3, "gpu_launches": n,
+                    "algorithmic_bytes": r["nbytes"], "timing": "CUDA graph of the timed launches",
+                    "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                 "frac": r["gbs"] / peaks["hbm_gbs"], "traffic": None, "peak_kind": kind},
+                }
+                del r
+        n = max(10, args.steps)
+        r = combine_run(4, n, warmup, local, world, clocks=False)
+        subs["split_combine_4k_S4"] = {
+            "value": r["gbs"] * world, "unit": "GB/s", "us_per_launch": r["ms"] * 1e3, "gpu_launches": n,
+            "algorithmic_bytes": r["nbytes"], "timing": "CUDA graph of the timed launches",
+            "roofline": {"bound": "hbm", "achieved": r["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": r["gbs"] / peaks["hbm_gbs"], "traffic": None, "peak_kind": kind},
+        }
+        del r
+        torch.cuda.empty_cache()
+    finally:
+        sampler.__exit__(None, None, None)
+    subs["clocks"] = sampler.summary()
+    return subs
+
+
+def attention_bench(args, world, rank, local):
+    from minicpm_b200.workloads import attention_kv_bytes
+
+    decode = args.workload.startswith("decode")
+    r = attention_run(args.workload, args.splits, args.steps, args.warmup, world, rank, local, args.num_seqs,
+                      graph=args.graph)
+    batch, out, stream = r["batch"], r["out"], r["stream"]
+    max_ms, total_flops, total_tokens = r["max_ms"], r["total_flops"], r["total_tokens"]
 
     # e2e: public operator API, host buffers, copies inside the timed region.
     e2e = None
     if not args.no_e2e:
-        e2e = e2e_pipelined(args, batch, out, splits, stream, world, total_flops, total_tokens)
+        e2e = e2e_pipelined(args, batch, out, args.splits, stream, world, total_flops, total_tokens)
 
     if args.verify:
-        verify_sharded(args, batch, out, world, rank, splits)
+        verify_sharded(args, batch, out, world, rank, args.splits)
+
+    subs = None
+    if args.workload == "chunked_prefill_16k" and not args.no_sub and not args.num_seqs:
+        del r["g"], r["out"]
+        out = None
+        torch.cuda.empty_cache()
+        subs = sub_benchmarks(args, world, rank, local)
 
     if rank != 0:
         return
     peaks, peak_kind = measured_peaks()
-    launch_ms = statistics.mean(per_launch)
-    achieved = local_flops / (launch_ms * 1e-3) / 1e12
-    traffic = None
-    tfile = ROOT / "profiles" / f"paged_attn_fwd_{args.workload}.traffic.json"
-    if tfile.exists():
-        try:
-            traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch")
-        except Exception:
-            traffic = None
+    launch_ms = r["launch_ms"]
+    achieved = r["local_flops"] / (launch_ms * 1e-3) / 1e12
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
@@ -805,51 +975,44 @@ def attention_bench(args, world, rank, local):
         else:
             cpu = {"value": flops_s / statistics.mean(ts) / 1e12, "unit": "TFLOP/s",
                    "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
-    l2_note = "inputs larger than L2 (KV %.0f MB + Q %.0f MB per GPU)" % (
-        g.kv_cache.numel() * 2 / 1e6 * (1 if world == 1 else 1), g.q.numel() * 2 / 1e6)
+    config = attention_config(args.workload, world, args.splits, args.num_seqs)
+    config["timing"] = "one CUDA graph of the K calls" if args.graph else "K calls launched from Python"
     line = {
         "metric": METRIC,
-        "value": value,
+        "value": r["value"],
         "unit": "TFLOP/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": max_ms / args.steps,
         "higher_is_better": True,
-        "scaling": "weak" if args.workload == "mixed_256" else "strong",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, random-permuted page table)",
-        "tokens_per_s": tokens_per_s,
-        "tc_peak_frac": value / world / peaks["bf16_tflops"],
-        "config": {
-            "workload": args.workload,
-            "seqs": len(all_q),
-            "query_tokens": total_tokens,
-            "causal_flops": total_flops,
-            "heads": "16q/2kv", "head_dim": 128, "page_size": 16,
-            "num_splits": resolved,
-            "parallelism": f"sequence-sharded x{world}",
-            "timing": "one CUDA graph of the K calls" if args.graph else "K calls launched from Python",
-            "l2": l2_note,
-        },
+        "tokens_per_s": r["tokens_per_s"],
+        "tc_peak_frac": r["value"] / world / peaks["bf16_tflops"],
+        "config": config,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": traffic_per_launch(args.workload),
                      "peak_kind": f"bf16_tflops (burst) of {peak_kind}",
                      "per_launch_ms": launch_ms, "launch": "schedule + attention kernels of one call"},
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "clocks": clocks.summary(),
-        "gpu_launches": args.steps * (2 + (1 if resolved > 1 else 0)),
+        "clocks": r["clocks"],
+        "gpu_launches": args.steps * (2 + (1 if r["resolved"] > 1 else 0)),
     }
+    if world > 1:
+        line["rank0_ms_per_step"] = sum(r["per_launch"]) / args.steps
     if decode:
         # Decode streams every K/V row once for a handful of query rows: the
         # bound is HBM, and the metric is the bytes moved per second.
+        total_bytes, local_bytes = r["total_bytes"], r["local_bytes"]
         gbs = total_bytes * args.steps / (max_ms * 1e-3) / 1e9
         achieved_gbs = local_bytes / (launch_ms * 1e-3) / 1e9
         line.update({
             "metric": "paged decode attention GB/s (K/V streamed once)", "value": gbs, "unit": "GB/s",
-            "tc_peak_frac": None, "decode_tokens_per_s": tokens_per_s,
+            "tc_peak_frac": None, "decode_tokens_per_s": r["tokens_per_s"],
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": None, "peak_kind": peak_kind,
                          "per_launch_ms": launch_ms, "launch": "schedule + attention (+ combine) kernels of one call"},
@@ -858,6 +1021,9 @@ def attention_bench(args, world, rank, local):
         if e2e:
             e2e["value"] = total_bytes * args.steps / (e2e["ms_per_step"] * args.steps * 1e-3) / 1e9
             e2e["unit"] = "GB/s"
+    if subs:
+        line["sub"] = subs
+        line["gpu_launches"] += sum(v.get("gpu_launches", 0) for v in subs.values() if isinstance(v, dict))
     print(json.dumps(line), flush=True)
 
 

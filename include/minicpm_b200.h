@@ -169,7 +169,10 @@ B200_API int32_t b200_attn_shape_supported(int32_t num_q_heads, int32_t num_kv_h
  * library until the process exits.  Calls whose scratch need
  * (b200_attn_workspace_bytes) exceeds it fail with B200_ERR_INVALID.  The
  * first call on a device looks up the array's device address (make it before
- * any stream capture).  All calls on a device share the array: calls that
+ * any stream capture) and keeps it for the life of the process: after a
+ * cudaDeviceReset (or anything else that destroys the device's primary
+ * context) that address is stale, so do not use this entry point across a
+ * device reset.  All calls on a device share the array: calls that
  * overlap on the GPU (other streams, other threads) race and must not be
  * issued.  No scratch byte needs to start at zero; every byte a call reads
  * it wrote first.  Allocates nothing.

@@ -847,6 +847,8 @@ int b200_paged_attn_fwd_noalloc(const B200AttnParams* p, void* stream) {
   {
     // Set-up, once per device, with that device current: the host-side name
     // g_static_scratch is only a stand-in, the kernel needs the device address.
+    // The address is kept for the life of the process (the header tells
+    // callers not to use this entry point across a device reset).
     std::lock_guard<std::mutex> lock(g_static_scratch_mu);
     if (!g_static_scratch_ptr[dev]) {
       void* ptr = nullptr;

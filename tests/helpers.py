@@ -72,6 +72,46 @@ def row_subset_batch(batch: AttentionBatch, seq: int, r0: int, r1: int) -> tuple
     return sub, slice(begin + r0, begin + r1)
 
 
+def sample_blocks(query_lens, block: int = 16) -> list[tuple[int, int, int]]:
+    """``(seq, r0, r1)`` row blocks: the first, middle and last ``block`` query
+    rows of every sequence (every row of a sequence shorter than 3 blocks)."""
+    picks = []
+    for seq, q_len in enumerate(query_lens):
+        if q_len <= 0:
+            continue
+        if q_len <= 3 * block:
+            picks.append((seq, 0, q_len))
+            continue
+        mid = (q_len - block) // 2
+        picks += [(seq, 0, block), (seq, mid, mid + block), (seq, q_len - block, q_len)]
+    return picks
+
+
+def sampled_oracle(batch: AttentionBatch, picks) -> tuple[torch.Tensor, torch.Tensor]:
+    """The oracle on the picked row blocks only, in one call.
+
+    Each block becomes a sequence of its own that keeps its rows' absolute
+    positions (KV length = the causal limit of its last row, same block-table
+    row).  Returns ``(want [N, H, D] fp32, row indices [N] into batch.q)``.
+    """
+    cu = batch.cu_seqlens_q.tolist()
+    qs, rows, tables, lens, qlens = [], [], [], [], []
+    for seq, r0, r1 in picks:
+        begin = cu[seq]
+        qs.append(batch.q[begin + r0 : begin + r1])
+        rows.append(torch.arange(begin + r0, begin + r1))
+        tables.append(batch.block_table[seq])
+        lens.append(batch.kv_lens[seq] - batch.query_lens[seq] + r1)
+        qlens.append(r1 - r0)
+    sub = AttentionBatch(
+        q=torch.cat(qs), kv_cache=batch.kv_cache, block_table=torch.stack(tables),
+        cu_seqlens_q=torch.tensor([0, *torch.tensor(qlens).cumsum(0).tolist()], dtype=torch.int32),
+        seqused_k=torch.tensor(lens, dtype=torch.int32), query_lens=qlens, kv_lens=lens,
+        softmax_scale=batch.softmax_scale, seq_ids=[batch.seq_ids[p[0]] for p in picks],
+    )
+    return oracle(sub), torch.cat(rows)
+
+
 def small_batch(query_lens, prefix_lens, **kw) -> AttentionBatch:
     return build_attention_batch(query_lens, [p + q for p, q in zip(prefix_lens, query_lens)], **kw)
 
@@ -84,6 +124,8 @@ __all__ = [
     "errors",
     "assert_close",
     "row_subset_batch",
+    "sample_blocks",
+    "sampled_oracle",
     "small_batch",
     "math",
 ]

@@ -14,9 +14,11 @@ import math
 import pytest
 import torch
 
-from helpers import ATOL_MAX, ATOL_MEAN, assert_close, errors, oracle, row_subset_batch, run_gpu, small_batch
+from helpers import (ATOL_MAX, ATOL_MEAN, assert_close, errors, oracle, run_gpu, sample_blocks, sampled_oracle,
+                     small_batch)
 from minicpm_b200 import _lib, iluvatar_attention, paged_split_kv_attention, split_kv_combine
-from minicpm_b200.workloads import build_attention_batch, correctness_batch, lengths_chunked_4k, lengths_chunked_16k
+from minicpm_b200.workloads import (build_attention_batch, correctness_batch, lengths_chunked_4k, lengths_chunked_16k,
+                                    lengths_mixed)
 
 pytestmark = pytest.mark.gpu
 
@@ -169,28 +171,57 @@ def test_deterministic_and_page_permutation_invariant():
     assert torch.equal(run_gpu(batch2, 1), a)
 
 
-def test_chunked_prefill_4k_subset_against_oracle():
+def test_chunked_prefill_4k_full_config_against_oracle():
+    """The whole 4K config (64 sequences, 512-token chunks, KV 1024-4096) at
+    S = 4 and 8 (the reference test's split counts,
+    tests/test_paged_split_kv.py:105-114) and auto: the first, middle and last
+    16 rows of every sequence against the oracle."""
     q, kv = lengths_chunked_4k()
-    batch = build_attention_batch(q[:6], kv[:6], seed=29)
-    want = oracle(batch)
-    for s in (1, 4, 8, 0):
-        assert_close(run_gpu(batch, s), want, f"4k subset S={s}")
+    batch = build_attention_batch(q, kv)
+    want, rows = sampled_oracle(batch, sample_blocks(q))
+    for s in (4, 8, 0):
+        assert_close(run_gpu(batch, s)[rows], want, f"4k S={s}")
     _no_device_error()
 
 
-def test_full_16k_config_sampled_rows_and_split_invariance():
-    """The 16K config at full size: sampled rows against the oracle, and
-    S = 1 / 4 / 8 agree with each other (a size-independent property)."""
+def test_full_16k_config_every_sequence_against_oracle():
+    """The 16K config at full size (64 sequences, 2048-token chunks, KV
+    8192-16384): the first, middle and last 16 rows of every sequence against
+    the oracle at S = 1, 4 and 8, and S = 4 / 8 against S = 1 over every row
+    (a size-independent property)."""
     q, kv = lengths_chunked_16k()
     batch = build_attention_batch(q, kv)
+    want, rows = sampled_oracle(batch, sample_blocks(q))
     outs = {s: run_gpu(batch, s) for s in (1, 4, 8)}
+    for s, got in outs.items():
+        assert_close(got[rows], want, f"16k S={s}")
     for s in (4, 8):
         mx, mn = errors(outs[s], outs[1])
         assert mx <= ATOL_MAX and mn <= 2e-4, (s, mx, mn)
-    for seq in (0, 31, 63):
-        for r0, r1 in ((0, 16), (1000, 1040), (2040, 2048)):
-            sub, rows = row_subset_batch(batch, seq, r0, r1)
-            assert_close(outs[1][rows], oracle(sub), f"16k seq{seq} rows{r0}:{r1}")
+    _no_device_error()
+
+
+def test_mixed_256_every_shard_against_oracle():
+    """The mixed batch (256 sequences, half decode rows, KV 512-16384) as the
+    8-GPU run shards it (LPT by causal FLOPs): every shard built as its rank
+    builds it and run on this GPU, sampled rows of every sequence and every
+    decode row against the oracle; then the whole batch in one call."""
+    from minicpm_b200.sharding import lpt_shard
+
+    q, kv = lengths_mixed()
+    shards = lpt_shard(q, kv, 8, 16, 128)
+    assert sorted(i for ids in shards for i in ids) == list(range(len(q)))
+    for rank, ids in enumerate(shards):
+        batch = build_attention_batch([q[i] for i in ids], [kv[i] for i in ids], seq_ids=ids)
+        want, rows = sampled_oracle(batch, sample_blocks(batch.query_lens))
+        picked = set(rows.tolist())
+        cu = batch.cu_seqlens_q.tolist()
+        assert all(cu[j] in picked for j, n in enumerate(batch.query_lens) if n == 1)  # every decode row is checked
+        for s in (0, 4):
+            assert_close(run_gpu(batch, s)[rows], want, f"mixed shard {rank} S={s}")
+    full = build_attention_batch(q, kv)
+    want, rows = sampled_oracle(full, sample_blocks(q))
+    assert_close(run_gpu(full, 0)[rows], want, "mixed whole batch")
     _no_device_error()
 
 

@@ -9,9 +9,10 @@ as ``b200_paged_attn_fwd`` with the scratch in a fixed-size device array
 inside the library instead of a caller-owned workspace.
 
 The GPU tests call it through the C ABI (ctypes, no torch in between) and
-check its output against the existing entry point's on two calls in a row,
-with and without a split KV axis (the split case keeps the partial outputs
-in the static array).  This file is named to be collected last.
+check its output against the existing entry point's on calls in a row that
+alternate prefill and decode batches, with and without a split KV axis and
+with the automatic split count (the split case keeps the partial outputs in
+the static array).  This file is named to be collected last.
 """
 
 from __future__ import annotations
@@ -68,18 +69,25 @@ def _assert_matches(got, want, tag):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("num_splits", [1, 4])
+@pytest.mark.parametrize("num_splits", [1, 4, 0])
 def test_noalloc_matches_existing_entry_point_two_calls(num_splits):
+    """Prefill and decode batches interleaved, so each call reads scratch that
+    a call of the other layout wrote (the decode kernel keeps item offsets, an
+    order list and fp32 partials there; the prefill kernel its work list and,
+    when split, the partial outputs and m / l)."""
     _lib.load().b200_paged_attn_fwd_noalloc.argtypes = [ctypes.POINTER(_lib.AttnParams), ctypes.c_void_p]
     first = correctness_batch().to("cuda")
     second = build_attention_batch([3, 200, 1], [40, 900, 77], seed=41).to("cuda")
-    want_first = _existing(first, num_splits)
-    want_second = _existing(second, num_splits)
-    # Two calls in a row on different batches, then the first batch again:
-    # each must match the workspace entry point despite the shared scratch.
-    _assert_matches(_noalloc(first, num_splits), want_first, "call 1")
-    _assert_matches(_noalloc(second, num_splits), want_second, "call 2")
-    _assert_matches(_noalloc(first, num_splits), want_first, "call 3")
+    # One query token per sequence, 8 query heads per KV head: the decode kernel.
+    decode = build_attention_batch([1] * 9, [5, 700, 2049, 16, 4096, 1, 300, 129, 1500], seed=43).to("cuda")
+    decode2 = build_attention_batch([1] * 3, [8000, 33, 257], seed=44).to("cuda")
+    calls = [("prefill 1", first), ("decode 1", decode), ("prefill 2", second), ("decode 2", decode2),
+             ("prefill 1 again", first), ("decode 1 again", decode)]
+    want = {tag: _existing(b, num_splits) for tag, b in calls}
+    # Calls in a row on different batches: each must match the workspace
+    # entry point despite the shared scratch.
+    for tag, b in calls:
+        _assert_matches(_noalloc(b, num_splits), want[tag], f"{tag} S={num_splits}")
     assert _lib.device_error() == _lib.DEVERR_NONE
 
 

@@ -875,7 +875,8 @@ def sub_benchmarks(args, world, rank, local) -> dict:
     """The rest of the metric, measured in the same run as the headline.
 
     * the 4K chunked-prefill config at S = auto / 4 / 8 (TFLOP/s, sharded like
-      the headline);
+      the headline; S is the most splits a query unit gets), and at S = 4 with
+      every query unit split (``_uniform``, the reference's rule);
     * the mixed 256-sequence batch (half decode rows), LPT-sharded over the
       ranks (TFLOP/s);
     * the RoPE + KV-cache write at rotary_dim 64 / 128 x NeoX / interleaved
@@ -890,11 +891,17 @@ def sub_benchmarks(args, world, rank, local) -> dict:
     sampler = ClockSampler(local)
     sampler.__enter__()
     try:
-        for workload, splits in (("chunked_prefill_4k", 0), ("chunked_prefill_4k", 4), ("chunked_prefill_4k", 8),
-                                 ("mixed_256", 0)):
-            r = attention_run(workload, splits, steps, warmup, world, rank, local, clocks=False)
+        for workload, splits, uniform in (("chunked_prefill_4k", 0, False), ("chunked_prefill_4k", 4, False),
+                                          ("chunked_prefill_4k", 8, False), ("chunked_prefill_4k", 4, True),
+                                          ("mixed_256", 0, False)):
+            if uniform:  # every query unit split `splits` ways: the reference's rule, for comparison
+                os.environ["B200_ATTN_SPLIT_UNIFORM"] = "1"
+            try:
+                r = attention_run(workload, splits, steps, warmup, world, rank, local, clocks=False)
+            finally:
+                os.environ.pop("B200_ATTN_SPLIT_UNIFORM", None)
             achieved = r["local_flops"] / (r["launch_ms"] * 1e-3) / 1e12
-            name = f"{workload}_S{splits}" if splits else f"{workload}_auto"
+            name = (f"{workload}_S{splits}" if splits else f"{workload}_auto") + ("_uniform" if uniform else "")
             subs[name] = {
                 "value": r["value"], "unit": "TFLOP/s", "ms_per_step": r["max_ms"] / steps, "steps": steps,
                 "gpu_launches": steps * (2 + (1 if r["resolved"] > 1 else 0)),

@@ -82,29 +82,40 @@ int encode_map(CUtensorMap* map, CUtensorMapDataType dt, cuuint32_t rank, const 
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Prefill workspace: the schedule's counters and per-sequence / per-query-unit
+// arrays, the work list, and (num_splits > 1) the split units' list and
+// partial outputs [slot][split][256 rows][head_dim] with m / l per row.
 struct WorkspaceLayout {
-  size_t count_off, tile_base_off, seq_off_off, units_off, o_off, m_off, l_off, total;
+  size_t count_off, tile_base_off, seq_off_off, qbase_off, qsplit_off, qslot_off, units_off, split_units_off;
+  size_t o_off, m_off, l_off, total;
   int capacity;
+  int64_t qunits_ub, slots_ub;
 };
 
 WorkspaceLayout attn_workspace_layout(int64_t total_q, int num_seqs, int hq, int hkv, int head_dim, int splits,
                                       int elt) {
   WorkspaceLayout w{};
   const int group = hkv > 0 ? hq / hkv : 1;
-  const int ppu = (group > 0 ? b200::kAttnTileM / group : 1) * b200::kAttnTilesPerUnit;
-  const int64_t tiles_ub = (total_q + ppu - 1) / (ppu > 0 ? ppu : 1) + num_seqs;
-  const int64_t cap = tiles_ub * hkv * splits;
+  const int ppu = std::max(group > 0 ? b200::kAttnTileM / group : 1, 1) * b200::kAttnTilesPerUnit;
+  w.qunits_ub = (total_q + ppu - 1) / ppu + num_seqs;
+  const int64_t cap = w.qunits_ub * hkv * splits;
   w.capacity = static_cast<int>(cap > 0x7fffffff ? 0x7fffffff : cap);
+  w.slots_ub = splits > 1 ? w.qunits_ub * hkv : 0;
+  const size_t qn = static_cast<size_t>(w.qunits_ub);
   w.count_off = 0;
   w.tile_base_off = 256;
   w.seq_off_off = align_up(w.tile_base_off + sizeof(int) * (num_seqs + 1), 256);
-  w.units_off = align_up(w.seq_off_off + sizeof(int) * num_seqs, 256);
-  w.o_off = align_up(w.units_off + sizeof(int4) * static_cast<size_t>(w.capacity), 256);
+  w.qbase_off = align_up(w.seq_off_off + sizeof(int) * num_seqs, 256);
+  w.qsplit_off = align_up(w.qbase_off + sizeof(int) * (qn + 1), 256);
+  w.qslot_off = align_up(w.qsplit_off + sizeof(int) * qn, 256);
+  w.units_off = align_up(w.qslot_off + sizeof(int) * qn, 256);
+  w.split_units_off = align_up(w.units_off + sizeof(int4) * static_cast<size_t>(w.capacity), 256);
+  w.o_off = align_up(w.split_units_off + sizeof(int4) * static_cast<size_t>(w.slots_ub), 256);
   w.m_off = w.o_off;
   w.l_off = w.o_off;
   w.total = w.o_off;
   if (splits > 1) {
-    const size_t rows = static_cast<size_t>(splits) * total_q * hq;
+    const size_t rows = static_cast<size_t>(w.slots_ub) * splits * b200::kUnitRows;
     w.m_off = align_up(w.o_off + rows * head_dim * elt, 256);
     w.l_off = align_up(w.m_off + rows * sizeof(float), 256);
     w.total = align_up(w.l_off + rows * sizeof(float), 256);
@@ -143,6 +154,14 @@ DecodeLayout decode_layout(int num_seqs, int hkv, int group, int max_k, int num_
 
 bool decode_shape_ok(int group, int hkv) {
   return (group == 4 || group == 8 || group == 16) && hkv <= b200::kDecMaxKvHeads;
+}
+
+// B200_ATTN_SPLIT_UNIFORM=1 splits every query unit num_splits ways (the
+// reference's rule) instead of only the units that are a large share of the
+// batch's work per SM; for measuring the split path and testing it at scale.
+bool uniform_splits() {
+  const char* e = getenv("B200_ATTN_SPLIT_UNIFORM");
+  return e && e[0] == '1';
 }
 
 // B200_ATTN_DECODE=0 sends decode batches through the prefill kernel instead.
@@ -451,10 +470,16 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   sa.pos_per_unit = ppt * b200::kAttnTilesPerUnit;
   sa.num_kv_heads = p->num_kv_heads;
   sa.num_splits = splits;
+  sa.uniform_splits = uniform_splits() ? 1 : 0;
+  sa.num_sms = sm_count();
   sa.capacity = w.capacity;
   sa.tile_base = reinterpret_cast<int*>(ws + w.tile_base_off);
   sa.seq_off = reinterpret_cast<int*>(ws + w.seq_off_off);
+  sa.qunit_base = reinterpret_cast<int*>(ws + w.qbase_off);
+  sa.qunit_split = reinterpret_cast<int*>(ws + w.qsplit_off);
+  sa.qunit_slot = reinterpret_cast<int*>(ws + w.qslot_off);
   sa.units = reinterpret_cast<int4*>(ws + w.units_off);
+  sa.split_units = reinterpret_cast<int4*>(ws + w.split_units_off);
   sa.unit_count = reinterpret_cast<int*>(ws + w.count_off);
   b200::attn_schedule_kernel<<<1, b200::kSchedThreads, 0, s>>>(sa);
   if (int r = check_launch("attn_schedule_kernel")) return r;
@@ -527,26 +552,36 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   if (int r = check_launch("paged_attn_fwd_kernel")) return r;
 
   if (splits > 1) {
-    B200CombineParams c{};
-    c.o_splits = ws + w.o_off;
-    c.m_splits = a.m_split;
-    c.l_splits = a.l_split;
+    // Combine of the split units' partials; the split-unit count is on the
+    // device, so the grid is a bound and the kernel loops up to the count.
+    b200::UnitCombineArgs c{};
+    c.o_part = a.o_split;
+    c.m_part = a.m_split;
+    c.l_part = a.l_split;
+    c.split_units = sa.split_units;
+    c.unit_count = sa.unit_count;
+    c.cu_q = p->cu_seqlens_q;
     c.out = p->out;
-    c.o_stride_h = p->head_dim;
-    c.o_stride_t = (int64_t)p->num_q_heads * p->head_dim;
-    c.o_stride_s = c.o_stride_t * p->total_q;
-    c.m_stride_h = c.l_stride_h = 1;
-    c.m_stride_t = c.l_stride_t = p->num_q_heads;
-    c.m_stride_s = c.l_stride_s = (int64_t)p->num_q_heads * p->total_q;
-    c.out_stride_t = p->out_stride_t;
-    c.out_stride_h = p->out_stride_h;
-    c.o_dtype = p->dtype;
-    c.out_dtype = p->dtype;
+    c.out_st = p->out_stride_t;
+    c.out_sh = p->out_stride_h;
+    c.len_i64 = sa.len_i64;
     c.num_splits = splits;
-    c.total_q = p->total_q;
-    c.num_heads = p->num_q_heads;
-    c.head_dim = p->head_dim;
-    return b200_split_combine(&c, stream);
+    c.group = group;
+    c.pos_per_tile = ppt;
+    c.pos_per_unit = sa.pos_per_unit;
+    const int rows_per_block = b200::kCombineThreads / (p->head_dim / 8);
+    const int64_t blocks_ub = (w.slots_ub * b200::kUnitRows + rows_per_block - 1) / rows_per_block;
+    const dim3 cgrid((unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks_ub, (int64_t)sm_count() * 8)));
+#define B200_UCOMB_S(T, D)                                                                                       \
+  if (splits <= 4) b200::unit_combine_kernel<T, D, 4><<<cgrid, b200::kCombineThreads, 0, s>>>(c);               \
+  else if (splits <= 8) b200::unit_combine_kernel<T, D, 8><<<cgrid, b200::kCombineThreads, 0, s>>>(c);          \
+  else b200::unit_combine_kernel<T, D, 16><<<cgrid, b200::kCombineThreads, 0, s>>>(c);
+#define B200_UCOMB_D(T)                                 \
+  if (p->head_dim == 64) { B200_UCOMB_S(T, 64) } else { B200_UCOMB_S(T, 128) }
+    if (bf16) { B200_UCOMB_D(__nv_bfloat16) } else { B200_UCOMB_D(__half) }
+#undef B200_UCOMB_D
+#undef B200_UCOMB_S
+    return check_launch("unit_combine_kernel");
   }
   return B200_OK;
 }

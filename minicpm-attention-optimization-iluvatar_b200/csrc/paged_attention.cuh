@@ -3,12 +3,19 @@
 // Semantics follow the reference Split-KV kernel
 // (kernels/triton_split_kv_paged.py:63-155 of the reference project):
 //   * query row i of sequence b sits at absolute position L_b - q_len_b + i;
-//   * split s of S covers keys [s * ceil(L/S), min((s + 1) * ceil(L/S), L));
-//   * a key is valid for a row iff it is inside the split and <= the row's
-//     absolute position; a row with no valid key keeps l = 0 and O = 0;
-//   * S == 1 writes the normalised output directly; S > 1 writes the
-//     normalised partial O (in the query dtype) plus m (natural-log units)
-//     and l, which b200_split_combine reduces.
+//   * a key is valid for a row iff it is inside the row's split and <= the
+//     row's absolute position; a row with no valid key keeps l = 0 and O = 0;
+//   * an unsplit unit writes the normalised output directly; a unit split
+//     s ways writes, per split, the normalised partial O (in the query
+//     dtype) plus m (natural-log units) and l, which unit_combine_kernel
+//     reduces with the weights of the reference's _split_kv_reduce.
+// Splits are chosen per query unit by the schedule kernel: the caller's
+// num_splits is the most any unit gets, and a unit is split only when it is a
+// large share of the batch's work per SM (so a batch that fills the GPU many
+// times over runs unsplit).  A unit split s ways covers its own key range
+// [0, min(L, last row's position + 1)) in s runs of whole 128-key tiles (the
+// reference splits [0, L) into ceil(L/S)-key runs; the combined output is the
+// same attention, within rounding).
 //
 // Work unit = (sequence, KV head, query-tile pair, split).  A query tile packs
 // the G = Hq / KH query heads that share one KV head with P = floor(128 / G)
@@ -58,6 +65,7 @@
 #include <type_traits>
 
 #include "sm100_ptx.cuh"
+#include "split_combine.cuh"
 
 namespace b200 {
 
@@ -99,11 +107,24 @@ enum : int {
   BAR_COUNT = BAR_DRAIN + 1
 };
 
-// A claimed unit as the producer publishes it: (seq, qunit, kvh, split),
-// then cu_q[seq], cu_q[seq + 1], seqused[seq] and a valid flag (0 ends the loop).
+// A claimed unit as the producer publishes it: (seq, qunit, kvh, split, the
+// unit's split count, its partial-output slot), then cu_q[seq], cu_q[seq + 1],
+// seqused[seq] and a valid flag (0 ends the loop).
 struct UnitEntry {
-  int seq, qunit, kvh, split, q_begin, q_end, seq_len, valid;
+  int seq, qunit, kvh, split, nsplit, slot, q_begin, q_end, seq_len, valid;
 };
+
+// Work-list entry: x = sequence, y = query unit, z = KV head | split << 16 |
+// split count << 24, w = partial-output slot of a split unit (-1 unsplit).
+__device__ __forceinline__ int4 pack_unit(int seq, int qunit, int kvh, int split, int nsplit, int slot) {
+  return make_int4(seq, qunit, kvh | (split << 16) | (nsplit << 24), slot);
+}
+__device__ __forceinline__ void unpack_unit(const int4 u, int& kvh, int& split, int& nsplit) {
+  kvh = u.z & 0xffff;
+  split = (u.z >> 16) & 0xff;
+  nsplit = (u.z >> 24) & 0xff;
+}
+constexpr int kUnitRows = 256;  // partial rows per split unit: 2 query tiles x 128 rows
 constexpr uint32_t kSmRing = BAR_COUNT * 8 + 16;  // after the barriers, the TMEM slot and the abort flag
 static_assert(kSmRing + kUnitRing * sizeof(UnitEntry) <= 512, "barrier area");
 
@@ -113,7 +134,7 @@ struct AttnKernelArgs {
   const void* seqused;
   void* out;
   void* o_split;
-  float* m_split;
+  float* m_split;    // [slots][num_splits][kUnitRows]
   float* l_split;
   const int4* units;
   const int* unit_count;
@@ -128,7 +149,7 @@ struct AttnKernelArgs {
   int pos_per_tile;   // P = floor(128 / G)
   int block_size;
   int num_blocks;
-  int num_splits;
+  int num_splits;     // the most splits any unit has (the partial buffers' split stride)
   int head_dim;       // 128, or 64 (the upper 64 columns of every tile are TMA zero fill)
   float scale_log2;   // softmax_scale * log2(e)
 };
@@ -166,8 +187,18 @@ struct UnitGeom {
   int q_abs_min;
 };
 
+// KV tiles of a query unit's whole causal key range [0, min(L, last row + 1)).
+__device__ __forceinline__ int qunit_full_tiles(int q_len, int seq_len, int qunit, int pos_per_unit) {
+  const int pos0 = qunit * pos_per_unit;
+  const int rows = min(pos_per_unit, q_len - pos0);
+  const int kv_end = min(max(seq_len, 0), seq_len - q_len + pos0 + rows);
+  return kv_end > 0 ? (kv_end + kAttnTileN - 1) / kAttnTileN : 0;
+}
+
+// Split `split` of `nsplit` covers whole tiles [split * tps, (split + 1) * tps)
+// of the unit's key range, tps = ceil(full tiles / nsplit).
 __device__ __forceinline__ UnitGeom unit_geometry(int q_begin, int q_end, int seq_len, int qunit, int split,
-                                                  int pos_per_unit, int num_splits) {
+                                                  int nsplit, int pos_per_unit) {
   UnitGeom u;
   u.q_begin = q_begin;
   u.q_len = q_end - q_begin;
@@ -175,13 +206,13 @@ __device__ __forceinline__ UnitGeom unit_geometry(int q_begin, int q_end, int se
   u.pos0 = qunit * pos_per_unit;
   const int rows = min(pos_per_unit, u.q_len - u.pos0);
   u.q_abs_min = seq_len - u.q_len + u.pos0;
-  const int q_abs_max = u.q_abs_min + rows - 1;
-  const int L = max(seq_len, 0);
-  const int split_size = (L + num_splits - 1) / num_splits;
-  u.split_begin = split * split_size;
-  u.split_end = min(u.split_begin + split_size, L);
-  u.kv_hi = min(u.split_end, q_abs_max + 1);
-  u.kv_lo = (u.split_begin / kAttnSlice) * kAttnSlice;
+  const int kv_end = max(min(max(seq_len, 0), u.q_abs_min + rows), 0);
+  const int n_full = (kv_end + kAttnTileN - 1) / kAttnTileN;
+  const int tps = nsplit > 1 ? (n_full + nsplit - 1) / nsplit : n_full;
+  u.split_begin = split * tps * kAttnTileN;
+  u.split_end = min(u.split_begin + tps * kAttnTileN, kv_end);
+  u.kv_hi = u.split_end;
+  u.kv_lo = u.split_begin;
   u.n_tiles = (u.kv_hi > u.split_begin) ? (u.kv_hi - u.kv_lo + kAttnTileN - 1) / kAttnTileN : 0;
   return u;
 }
@@ -285,6 +316,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     e.qunit = ring[r].qunit;
     e.kvh = ring[r].kvh;
     e.split = ring[r].split;
+    e.nsplit = ring[r].nsplit;
+    e.slot = ring[r].slot;
     e.q_begin = ring[r].q_begin;
     e.q_end = ring[r].q_end;
     e.seq_len = ring[r].seq_len;
@@ -292,7 +325,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     return true;
   };
   auto geometry = [&](const UnitEntry& e) {
-    return unit_geometry(e.q_begin, e.q_end, e.seq_len, e.qunit, e.split, ppu, a.num_splits);
+    return unit_geometry(e.q_begin, e.q_end, e.seq_len, e.qunit, e.split, e.nsplit, ppu);
   };
 
   if (warp < 4) {
@@ -319,8 +352,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int4 un = a.units[u];
           e.seq = un.x;
           e.qunit = un.y;
-          e.kvh = un.z;
-          e.split = un.w;
+          unpack_unit(un, e.kvh, e.split, e.nsplit);
+          e.slot = un.w;
           e.q_begin = load_index(a.cu_q, e.seq, a.len_i64);
           e.q_end = load_index(a.cu_q, e.seq + 1, a.len_i64);
           e.seq_len = load_index(a.seqused, e.seq, a.len_i64);
@@ -334,6 +367,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             ring[r].qunit = e.qunit;
             ring[r].kvh = e.kvh;
             ring[r].split = e.split;
+            ring[r].nsplit = e.nsplit;
+            ring[r].slot = e.slot;
             ring[r].q_begin = e.q_begin;
             ring[r].q_end = e.q_end;
             ring[r].seq_len = e.seq_len;
@@ -727,10 +762,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float inv = 1.f / fmaxf(l, 1e-20f);
       const int tok = ug.q_begin + row_pos;
       T* dst;
-      if (a.num_splits == 1) {
+      if (e.nsplit <= 1) {
         dst = static_cast<T*>(a.out) + static_cast<int64_t>(tok) * a.out_st + static_cast<int64_t>(row_head) * a.out_sh;
       } else {
-        const int64_t rowi = (static_cast<int64_t>(e.split) * a.total_q + tok) * a.num_q_heads + row_head;
+        const int64_t rowi = (static_cast<int64_t>(e.slot) * a.num_splits + e.split) * kUnitRows + t * kAttnTileM + row;
         dst = static_cast<T*>(a.o_split) + rowi * a.head_dim;
         if (row_valid) {
           a.m_split[rowi] = (l > 0.f) ? m_used * 0.69314718055994530942f : -INFINITY;
@@ -776,6 +811,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 // ---------------------------------------------------------------------------
 // Device-side work list, built by one block with no host synchronisation.
+//
+// Splits: a query unit's split count s is chosen here, at most the caller's
+// num_splits.  With W the KV tiles of all (query unit, KV head) pairs, a unit
+// of n tiles is split into s = ceil(n * kSplitBalance * SMs / W) runs (at
+// least kMinSplitTiles tiles each, none empty): a unit is split only when it
+// is more than 1/kSplitBalance of one SM's share of the batch, i.e. when the
+// batch is too small to keep every SM busy to the end without it.  The
+// uniform mode splits every unit num_splits ways (one run of whole tiles per
+// split, none empty), as the reference splits every query block.
+//
 // Order: sequences by estimated work, heaviest first (a bucket sort on a log
 // scale); inside a sequence, query units from the last (most keys) to the
 // first, the KV heads and splits of one query unit side by side.  The
@@ -791,6 +836,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 constexpr int kSchedThreads = 1024;
 constexpr int kSchedBuckets = 2048;
 constexpr float kSchedBucketsPerOctave = 46.0f;  // 2^44 (the largest work estimate) -> bucket 2024
+constexpr int kSplitBalance = 2;   // split units larger than half of one SM's share of the batch
+constexpr int kMinSplitTiles = 2;  // KV tiles each split keeps at least
 
 struct SchedArgs {
   const void* cu_q;
@@ -799,12 +846,18 @@ struct SchedArgs {
   int num_seqs;
   int pos_per_unit;  // query positions per work unit
   int num_kv_heads;
-  int num_splits;
+  int num_splits;    // the most splits a query unit may get
+  int uniform_splits;  // 1: every query unit is split num_splits ways
+  int num_sms;
   int capacity;
-  int* tile_base;  // [num_seqs + 1]: query units per sequence, exclusive prefix
-  int* seq_off;    // [num_seqs]: first slot of each sequence's units in the work list
+  int* tile_base;    // [num_seqs + 1]: query units per sequence, exclusive prefix
+  int* seq_off;      // [num_seqs]: first slot of each sequence's units in the work list
+  int* qunit_base;   // [query units + 1]: work units (splits x KV heads) per query unit, exclusive prefix
+  int* qunit_split;  // [query units]: splits of each query unit
+  int* qunit_slot;   // [query units]: index among the split query units, -1 if not split
   int4* units;
-  int* unit_count;  // [0] units, [1] claim counter of the attention kernel
+  int4* split_units;  // [split query units x KV heads]: (seq, qunit, kvh, splits), read by the combine
+  int* unit_count;    // [0] units, [1] claim counter of the attention kernel, [2] split-unit slots
 };
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& total) {
@@ -863,10 +916,37 @@ __device__ __forceinline__ int seq_bucket(const SchedArgs& a, int b, int units) 
   return min(kSchedBuckets - 1, max(0, static_cast<int>(__log2f(work) * kSchedBucketsPerOctave)));
 }
 
+// Last index i in [0, n) with v[i] <= x (v non-decreasing, v[0] <= x).
+__device__ __forceinline__ int upper_index(const int* v, int n, int x) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (v[mid] <= x) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Splits of a query unit whose whole key range has n tiles (see above).
+__device__ __forceinline__ int qunit_splits(const SchedArgs& a, int n, long long total_tiles) {
+  if (a.num_splits <= 1 || n <= 1) return 1;
+  long long s;
+  if (a.uniform_splits) {
+    s = min(a.num_splits, n);
+  } else {
+    const long long want = (static_cast<long long>(n) * kSplitBalance * a.num_sms + total_tiles - 1) /
+                           max(total_tiles, 1ll);
+    s = min(min(static_cast<long long>(a.num_splits), want), static_cast<long long>(n / kMinSplitTiles));
+  }
+  if (s <= 1) return 1;
+  const int tps = (n + static_cast<int>(s) - 1) / static_cast<int>(s);  // whole tiles per split
+  return (n + tps - 1) / tps;                                             // no split left empty
+}
+
 __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const SchedArgs a) {
   __shared__ int hist[kSchedBuckets];
   __shared__ int warp_sums[32];
-  __shared__ int s_total_tiles;
+  __shared__ int s_total_qunits;
+  __shared__ unsigned long long s_total_tiles;
   griddep_launch_dependents();  // the attention grid may launch; it waits for this one
 
   // 1. query units per sequence, exclusive prefix over sequences.
@@ -885,46 +965,76 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   }
   if (threadIdx.x == 0) {
     a.tile_base[a.num_seqs] = carry;
-    s_total_tiles = carry;
+    s_total_qunits = carry;
+    s_total_tiles = 0ull;
   }
   for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;
   __syncthreads();
+  const int nq = s_total_qunits;
 
-  const int per_tile = a.num_kv_heads * a.num_splits;
-  const int total_units = min(s_total_tiles * per_tile, a.capacity);
+  // 2. KV tiles of each query unit's whole key range (kept in qunit_split for
+  // now) and their sum over query units and KV heads.
+  unsigned long long my_tiles = 0;
+  for (int j = threadIdx.x; j < nq; j += kSchedThreads) {
+    const int seq = upper_index(a.tile_base, a.num_seqs, j);
+    const int ql = load_index(a.cu_q, seq + 1, a.len_i64) - load_index(a.cu_q, seq, a.len_i64);
+    const int n = qunit_full_tiles(ql, load_index(a.seqused, seq, a.len_i64), j - a.tile_base[seq], a.pos_per_unit);
+    a.qunit_split[j] = n;
+    my_tiles += static_cast<unsigned long long>(n);
+  }
+  atomicAdd(&s_total_tiles, my_tiles);
+  __syncthreads();
+  const long long total_tiles = static_cast<long long>(s_total_tiles) * a.num_kv_heads;
 
-  // 2. units per work bucket.
+  // 3. splits per query unit; work units and split slots, exclusive prefixes.
+  int ucarry = 0, scarry = 0;
+  for (int base = 0; base < nq; base += kSchedThreads) {
+    const int j = base + threadIdx.x;
+    int s = 1;
+    if (j < nq) s = qunit_splits(a, a.qunit_split[j], total_tiles);
+    int utotal, stotal;
+    const int ubefore = block_exclusive_scan(j < nq ? s * a.num_kv_heads : 0, warp_sums, utotal);
+    const int sbefore = block_exclusive_scan(j < nq && s > 1 ? 1 : 0, warp_sums, stotal);
+    if (j < nq) {
+      a.qunit_split[j] = s;
+      a.qunit_base[j] = ucarry + ubefore;
+      a.qunit_slot[j] = s > 1 ? scarry + sbefore : -1;
+    }
+    ucarry += utotal;
+    scarry += stotal;
+  }
+  if (threadIdx.x == 0) a.qunit_base[nq] = ucarry;
+  __syncthreads();
+  const int total_units = min(ucarry, a.capacity);
+
+  // 4. units per work bucket; each sequence takes a contiguous range of its bucket.
+  auto seq_units = [&](int b) { return a.qunit_base[a.tile_base[b + 1]] - a.qunit_base[a.tile_base[b]]; };
   for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
     const int qt = a.tile_base[b + 1] - a.tile_base[b];
-    if (qt > 0) atomicAdd(&hist[seq_bucket(a, b, qt)], qt * per_tile);
+    if (qt > 0) atomicAdd(&hist[seq_bucket(a, b, qt)], seq_units(b));
   }
   __syncthreads();
-  // 3. bucket offsets, heaviest bucket first.
   buckets_to_offsets_desc(hist, warp_sums);
   __syncthreads();
-  // 4. each sequence takes a contiguous range of its bucket.
   for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
     const int qt = a.tile_base[b + 1] - a.tile_base[b];
-    if (qt > 0) a.seq_off[b] = atomicAdd(&hist[seq_bucket(a, b, qt)], qt * per_tile);
+    if (qt > 0) a.seq_off[b] = atomicAdd(&hist[seq_bucket(a, b, qt)], seq_units(b));
   }
   __syncthreads();
-  // 5. scatter: unit u = (query tile, KV head, split) in natural order goes to
-  // its sequence's range, last query unit first.
+  // 5. scatter: unit u (query unit j, then KV head, then split) goes to its
+  // sequence's range, the sequence's last query unit first.
   for (int u = threadIdx.x; u < total_units; u += kSchedThreads) {
-    const int tile = u / per_tile;
-    const int rem = u - tile * per_tile;
-    const int kvh = rem / a.num_splits;
-    const int split = rem - kvh * a.num_splits;
-    int lo = 0, hi = a.num_seqs - 1;  // last seq with tile_base[seq] <= tile
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (a.tile_base[mid] <= tile) lo = mid; else hi = mid - 1;
-    }
-    const int seq = lo;
-    const int qtile = tile - a.tile_base[seq];
-    const int qt = a.tile_base[seq + 1] - a.tile_base[seq];
-    const int slot = a.seq_off[seq] + (qt - 1 - qtile) * per_tile + rem;
-    if (slot < a.capacity) a.units[slot] = make_int4(seq, qtile, kvh, split);
+    const int j = upper_index(a.qunit_base, nq, u);
+    const int seq = upper_index(a.tile_base, a.num_seqs, j);
+    const int s = a.qunit_split[j];
+    const int rem = u - a.qunit_base[j];
+    const int kvh = rem / s;
+    const int split = rem - kvh * s;
+    const int slot = s > 1 ? a.qunit_slot[j] * a.num_kv_heads + kvh : -1;
+    const int qunit = j - a.tile_base[seq];
+    const int pos = a.seq_off[seq] + (a.qunit_base[a.tile_base[seq + 1]] - a.qunit_base[j + 1]) + rem;
+    if (pos < a.capacity) a.units[pos] = pack_unit(seq, qunit, kvh, split, s, slot);
+    if (s > 1 && split == 0) a.split_units[slot] = make_int4(seq, qunit, kvh, s);
   }
   __syncthreads();
   // 6. the schedule's tail, its last kSchedThreads units, by KV-tile count
@@ -937,9 +1047,10 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   int bucket = 0;
   if (mine) {
     unit = a.units[tail0 + threadIdx.x];
+    int kvh, split, nsplit;
+    unpack_unit(unit, kvh, split, nsplit);
     const UnitGeom g = unit_geometry(load_index(a.cu_q, unit.x, a.len_i64), load_index(a.cu_q, unit.x + 1, a.len_i64),
-                                     load_index(a.seqused, unit.x, a.len_i64), unit.y, unit.w, a.pos_per_unit,
-                                     a.num_splits);
+                                     load_index(a.seqused, unit.x, a.len_i64), unit.y, split, nsplit, a.pos_per_unit);
     bucket = min(g.n_tiles, kSchedBuckets - 1);
   }
   for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;
@@ -952,6 +1063,57 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   if (threadIdx.x == 0) {
     a.unit_count[0] = total_units;
     a.unit_count[1] = 0;  // claim counter of the persistent attention kernel
+    a.unit_count[2] = scarry * a.num_kv_heads;  // split-unit slots for the combine
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Combine of the split units' partials: one (token, head) row of a split unit
+// per D/8 threads, over a grid-stride loop whose bound (the split-unit count)
+// the schedule kernel left on the device; a call without split units costs
+// one launch that exits at once.  Row r of a unit is query tile r / 128, tile
+// row r % 128 = (position, head) as in the attention kernel; padding rows and
+// positions past the sequence's query rows are skipped.
+// ---------------------------------------------------------------------------
+struct UnitCombineArgs {
+  const void* o_part;      // [slots][num_splits][kUnitRows][head_dim], query dtype
+  const float* m_part;     // [slots][num_splits][kUnitRows]
+  const float* l_part;
+  const int4* split_units;
+  const int* unit_count;   // [2] = slots
+  const void* cu_q;
+  void* out;
+  int64_t out_st, out_sh;
+  int len_i64;
+  int num_splits;
+  int group;
+  int pos_per_tile;
+  int pos_per_unit;
+};
+
+template <typename T, int D, int kS>
+__global__ void __launch_bounds__(kCombineThreads) unit_combine_kernel(const UnitCombineArgs a) {
+  constexpr int kThreadsPerRow = D / 8;
+  constexpr int kRowsPerBlock = kCombineThreads / kThreadsPerRow;
+  const int64_t rows = static_cast<int64_t>(a.unit_count[2]) * kUnitRows;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock; base < rows;
+       base += static_cast<int64_t>(gridDim.x) * kRowsPerBlock) {
+    const int64_t row_raw = base + threadIdx.x / kThreadsPerRow;
+    const bool in_range = row_raw < rows;  // threads past the end still take part in the shuffles
+    const int64_t row = in_range ? row_raw : rows - 1;
+    const int slot = static_cast<int>(row / kUnitRows);
+    const int ur = static_cast<int>(row - static_cast<int64_t>(slot) * kUnitRows);
+    const int4 su = a.split_units[slot];  // (seq, qunit, kvh, splits)
+    const int t = ur / kAttnTileM, r = ur % kAttnTileM;
+    const int q_begin = load_index(a.cu_q, su.x, a.len_i64);
+    const int q_len = load_index(a.cu_q, su.x + 1, a.len_i64) - q_begin;
+    const int pos = su.y * a.pos_per_unit + t * a.pos_per_tile + r / a.group;
+    const bool valid = in_range && r < a.group * a.pos_per_tile && pos < q_len;
+    const int64_t prow = static_cast<int64_t>(slot) * a.num_splits * kUnitRows + ur;
+    const int64_t tok = q_begin + pos, head = static_cast<int64_t>(su.z) * a.group + r % a.group;
+    combine_row<T, T, D, kS>(static_cast<const T*>(a.o_part) + prow * D, static_cast<int64_t>(kUnitRows) * D,
+                             a.m_part + prow, kUnitRows, a.l_part + prow, kUnitRows, su.w,
+                             static_cast<T*>(a.out) + tok * a.out_st + head * a.out_sh, valid);
   }
 }
 

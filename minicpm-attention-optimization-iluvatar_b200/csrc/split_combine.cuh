@@ -140,35 +140,29 @@ __device__ __forceinline__ void SplitChunk8<__half>::to_float(float (&v)[8]) con
 // ...), the group reduces the maximum and forms each split's weight, and the
 // weights reach every thread of the group by shuffles.  A split with l = 0
 // carries weight -1 and is left out by selection (its O, whatever it holds,
-// never reaches the sum).
+// never reaches the sum).  `o`, `m`, `l` point at split 0 of the row; every
+// thread of the group calls this (the shuffles need all of them), and only
+// threads with `valid` store.
 template <typename TO, typename TOut, int D, int kS>
-__global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const CombineArgs a) {
+__device__ __forceinline__ void combine_row(const TO* o, int64_t o_ss, const float* m, int64_t m_ss, const float* l,
+                                            int64_t l_ss, int num_splits, TOut* dst, bool valid) {
   constexpr int kThreadsPerRow = D / 8;
-  constexpr int kRowsPerBlock = kCombineThreads / kThreadsPerRow;
   constexpr int kPer = (kS + kThreadsPerRow - 1) / kThreadsPerRow;  // splits whose m / l one thread loads
   const int sub = threadIdx.x % kThreadsPerRow;
-  const int64_t nrows = static_cast<int64_t>(a.total_q) * a.num_heads;
-  const int64_t row_raw = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / kThreadsPerRow;
-  const bool valid = row_raw < nrows;  // threads past the end still take part in the shuffles
-  const int64_t row = valid ? row_raw : nrows - 1;
-  const int64_t t = row / a.num_heads;
-  const int64_t h = row - t * a.num_heads;
   const int d0 = sub * 8;
-
-  const TO* o = static_cast<const TO*>(a.o) + t * a.o_st + h * a.o_sh + d0;
   SplitChunk8<TO> raw[kS];
 #pragma unroll
   for (int s = 0; s < kS; ++s)
-    if (s < a.num_splits) raw[s].load(o + s * a.o_ss);
+    if (s < num_splits) raw[s].load(o + s * o_ss + d0);
   float mk[kPer], lk[kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const int s = sub + k * kThreadsPerRow;
     mk[k] = -INFINITY;
     lk[k] = 0.f;
-    if (s < a.num_splits) {
-      mk[k] = __ldg(a.m + s * a.m_ss + t * a.m_st + h * a.m_sh);
-      lk[k] = __ldg(a.l + s * a.l_ss + t * a.l_st + h * a.l_sh);
+    if (s < num_splits) {
+      mk[k] = __ldg(m + s * m_ss);
+      lk[k] = __ldg(l + s * l_ss);
     }
   }
   float m_max = mk[0];
@@ -184,7 +178,7 @@ __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const Co
   float denom = 0.f;
 #pragma unroll
   for (int s = 0; s < kS; ++s) {
-    if (s < a.num_splits) {
+    if (s < num_splits) {
       const float w = __shfl_sync(0xffffffffu, wk[s / kThreadsPerRow], s % kThreadsPerRow, kThreadsPerRow);
       if (w >= 0.f) {
         float v[8];
@@ -198,7 +192,23 @@ __global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const Co
   const float inv = 1.f / fmaxf(denom, 1e-20f);
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] *= inv;
-  if (valid) store8<TOut>(static_cast<TOut*>(a.out) + t * a.out_st + h * a.out_sh + d0, acc);
+  if (valid) store8<TOut>(dst + d0, acc);
+}
+
+// The reduce of caller-supplied partials [S, T, H, D] (b200_split_combine).
+template <typename TO, typename TOut, int D, int kS>
+__global__ void __launch_bounds__(kCombineThreads) split_combine_kernel(const CombineArgs a) {
+  constexpr int kThreadsPerRow = D / 8;
+  constexpr int kRowsPerBlock = kCombineThreads / kThreadsPerRow;
+  const int64_t nrows = static_cast<int64_t>(a.total_q) * a.num_heads;
+  const int64_t row_raw = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + threadIdx.x / kThreadsPerRow;
+  const bool valid = row_raw < nrows;  // threads past the end still take part in the shuffles
+  const int64_t row = valid ? row_raw : nrows - 1;
+  const int64_t t = row / a.num_heads;
+  const int64_t h = row - t * a.num_heads;
+  combine_row<TO, TOut, D, kS>(static_cast<const TO*>(a.o) + t * a.o_st + h * a.o_sh, a.o_ss,
+                               a.m + t * a.m_st + h * a.m_sh, a.m_ss, a.l + t * a.l_st + h * a.l_sh, a.l_ss,
+                               a.num_splits, static_cast<TOut*>(a.out) + t * a.out_st + h * a.out_sh, valid);
 }
 
 }  // namespace b200

@@ -184,18 +184,56 @@ def test_chunked_prefill_4k_full_config_against_oracle():
     _no_device_error()
 
 
+def _split_slots() -> int:
+    """Split-unit slots the last call's schedule kernel made (its workspace counter)."""
+    dev = torch.cuda.current_device()
+    ws = _lib._workspaces[(dev, torch.cuda.current_stream().cuda_stream)]
+    return int(ws[:12].cpu().view(torch.int32)[2])
+
+
+def test_split_policy_splits_small_batches_only():
+    """num_splits is the most any query unit gets: the reference's third unit
+    case (few sequences, long keys) is split, the 4K config (13 waves of units
+    on 148 SMs) is not."""
+    ql, pre = REFERENCE_CASES[2]
+    small = small_batch(ql, pre, seed=20260930)
+    run_gpu(small, 4)
+    assert _split_slots() > 0
+    q, kv = lengths_chunked_4k()
+    run_gpu(build_attention_batch(q, kv), 4)
+    assert _split_slots() == 0
+
+
+@pytest.mark.parametrize("splits", [4, 8, 16])
+def test_uniform_splits_4k_against_oracle(monkeypatch, splits):
+    """B200_ATTN_SPLIT_UNIFORM=1 splits every query unit of the 4K config
+    `splits` ways (the reference's rule): the split path at full size, every
+    sequence's sampled rows against the oracle."""
+    monkeypatch.setenv("B200_ATTN_SPLIT_UNIFORM", "1")
+    q, kv = lengths_chunked_4k()
+    batch = build_attention_batch(q, kv)
+    want, rows = sampled_oracle(batch, sample_blocks(q))
+    got = run_gpu(batch, splits)
+    assert _split_slots() == 64 * 16 * 2  # every (query unit, KV head) of the batch
+    assert_close(got[rows], want, f"4k uniform S={splits}")
+    _no_device_error()
+
+
 def test_full_16k_config_every_sequence_against_oracle():
     """The 16K config at full size (64 sequences, 2048-token chunks, KV
     8192-16384): the first, middle and last 16 rows of every sequence against
-    the oracle at S = 1, 4 and 8, and S = 4 / 8 against S = 1 over every row
-    (a size-independent property)."""
+    the oracle at S = 1, 4 and 8 and with every query unit split 4 ways, and
+    the split runs against S = 1 over every row (a size-independent property)."""
     q, kv = lengths_chunked_16k()
     batch = build_attention_batch(q, kv)
     want, rows = sampled_oracle(batch, sample_blocks(q))
     outs = {s: run_gpu(batch, s) for s in (1, 4, 8)}
+    with pytest.MonkeyPatch.context() as mp:  # every query unit split 4 ways
+        mp.setenv("B200_ATTN_SPLIT_UNIFORM", "1")
+        outs["4u"] = run_gpu(batch, 4)
     for s, got in outs.items():
         assert_close(got[rows], want, f"16k S={s}")
-    for s in (4, 8):
+    for s in (4, 8, "4u"):
         mx, mn = errors(outs[s], outs[1])
         assert mx <= ATOL_MAX and mn <= 2e-4, (s, mx, mn)
     _no_device_error()

@@ -147,7 +147,7 @@ B200_API int b200_paged_attn_fwd(const B200AttnParams* params, void* stream);
 
 /*
  * 1 if b200_paged_attn_fwd runs this head shape and element type, else 0:
- * q/k/v/out F16 or BF16, head_dim 64 or 128, num_q_heads a multiple of
+ * q/k/v/out F16 or BF16, head_dim 64, 128 or 256, num_q_heads a multiple of
  * num_kv_heads with at most 128 query heads per KV head.  The dispatcher and
  * the service route other shapes to their baseline kernel before calling in,
  * as they route the unsupported features of kernels/attention.py:99-110 and

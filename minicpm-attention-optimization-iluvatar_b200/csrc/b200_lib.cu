@@ -96,7 +96,8 @@ WorkspaceLayout attn_workspace_layout(int64_t total_q, int num_seqs, int hq, int
                                       int elt) {
   WorkspaceLayout w{};
   const int group = hkv > 0 ? hq / hkv : 1;
-  const int ppu = std::max(group > 0 ? b200::kAttnTileM / group : 1, 1) * b200::kAttnTilesPerUnit;
+  // head_dim 256: one query tile per unit, else two.
+  const int ppu = std::max(group > 0 ? b200::kAttnTileM / group : 1, 1) * (head_dim == 256 ? 1 : b200::kAttnTilesPerUnit);
   w.qunits_ub = (total_q + ppu - 1) / ppu + num_seqs;
   const int64_t cap = w.qunits_ub * hkv * splits;
   w.capacity = static_cast<int>(cap > 0x7fffffff ? 0x7fffffff : cap);
@@ -185,8 +186,9 @@ int auto_splits(int32_t total_q, int32_t num_seqs, int32_t hq, int32_t hkv, int3
 }
 
 // Decode batch: schedule (items per sequence), persistent decode kernel, combine.
-// Per KV head: (d, key % 8, half of head_dim, key / 8 in the page, page); one
-// box = a 16-key page slice with both halves (4 KB).  Needs num_kv_heads <=
+// Per KV head: (d, key % 8, 64-column part of head_dim, key / 8 in the page,
+// page); one box = a 16-key page slice with two parts (4 KB): the whole row at
+// head_dim 128, one 128-column half of it at head_dim 256.  Needs num_kv_heads <=
 // kMaxHeadMaps and block_size % 16 == 0.
 int encode_kv_head_maps(const B200AttnParams* p, CUtensorMapDataType dt, b200::KvHeadMaps* maps) {
   const int elt = 2;
@@ -196,7 +198,8 @@ int encode_kv_head_maps(const B200AttnParams* p, CUtensorMapDataType dt, b200::K
       const uint8_t* base = static_cast<const uint8_t*>(kv ? p->v : p->k) +
                             (int64_t)h * (kv ? p->v_stride_head : p->k_stride_head) * elt;
       const int64_t st = kv ? p->v_stride_tok : p->k_stride_tok, sb = kv ? p->v_stride_block : p->k_stride_block;
-      const cuuint64_t dims[5] = {64, 8, 2, (cuuint64_t)(p->block_size / 8), (cuuint64_t)p->num_blocks};
+      const cuuint64_t dims[5] = {64, 8, (cuuint64_t)(p->head_dim / 64), (cuuint64_t)(p->block_size / 8),
+                                  (cuuint64_t)p->num_blocks};
       const cuuint64_t strides[4] = {(cuuint64_t)(st * elt), 128, (cuuint64_t)(8 * st * elt), (cuuint64_t)(sb * elt)};
       const cuuint32_t box[5] = {64, 8, 2, 2, 1};
       if (int r = encode_map(kv ? &maps->v[h] : &maps->k[h], dt, 5, base, dims, strides, box, kv ? "v" : "k")) return r;
@@ -312,7 +315,7 @@ int32_t b200_attn_shape_supported(int32_t num_q_heads, int32_t num_kv_heads, int
   if (dtype != B200_DTYPE_BF16 && dtype != B200_DTYPE_F16) return 0;
   if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return 0;
   if (num_q_heads / num_kv_heads > b200::kAttnTileM) return 0;
-  return head_dim == 64 || head_dim == b200::kAttnHeadDim;
+  return head_dim == 64 || head_dim == b200::kAttnHeadDim || head_dim == 256;
 }
 
 size_t b200_attn_workspace_bytes(int32_t total_q, int32_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
@@ -394,8 +397,8 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   // real 64-element rows, so the second 64-column half of every Q, K and V
   // box lies outside them and TMA fills it with zeros; S and P V are then
   // exactly those of head_dim 64, and the epilogue stores 64 columns.
-  if (p->head_dim != b200::kAttnHeadDim && p->head_dim != 64)
-    return fail(B200_ERR_UNSUPPORTED, "head_dim %d: the sm_100a kernel handles head_dim 64 and 128", p->head_dim);
+  // head_dim 256 runs the kernel's wide variant (one query tile per unit).
+  const bool wide = p->head_dim == 256;
   const int group = p->num_q_heads / p->num_kv_heads;
   if (group > b200::kAttnTileM)
     return fail(B200_ERR_UNSUPPORTED, "query heads per KV head (%d) must be at most 128", group);
@@ -453,7 +456,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Per-KV-head maps (4 KB boxes) when they fit; they assume full 128-column rows.
-  const bool head_maps = p->num_kv_heads <= b200::kMaxHeadMaps && p->head_dim == b200::kAttnHeadDim;
+  const bool head_maps = p->num_kv_heads <= b200::kMaxHeadMaps && p->head_dim != 64;
   b200::KvHeadMaps maps;
   if (head_maps) {
     if (int r = encode_kv_head_maps(p, dt, &maps)) return r;
@@ -467,7 +470,7 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   sa.seqused = p->seqused_k;
   sa.len_i64 = p->seqlen_dtype == B200_DTYPE_I64;
   sa.num_seqs = p->num_seqs;
-  sa.pos_per_unit = ppt * b200::kAttnTilesPerUnit;
+  sa.pos_per_unit = ppt * (wide ? 1 : b200::kAttnTilesPerUnit);
   sa.num_kv_heads = p->num_kv_heads;
   sa.num_splits = splits;
   sa.uniform_splits = uniform_splits() ? 1 : 0;
@@ -542,12 +545,15 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   };
   const bool bf16 = p->dtype == B200_DTYPE_BF16;
   int lr;
-  if (head_maps)
-    lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, true>, tm_q, maps, a)
-              : launch(b200::paged_attn_fwd_kernel<__half, true>, tm_q, maps, a);
-  else
-    lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, false>, tm_q, maps, a)
-              : launch(b200::paged_attn_fwd_kernel<__half, false>, tm_q, maps, a);
+#define B200_ATTN_LAUNCH(HM, WIDE)                                                                 \
+  lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, HM, WIDE>, tm_q, maps, a)          \
+            : launch(b200::paged_attn_fwd_kernel<__half, HM, WIDE>, tm_q, maps, a);
+  if (wide) {
+    if (head_maps) { B200_ATTN_LAUNCH(true, true) } else { B200_ATTN_LAUNCH(false, true) }
+  } else {
+    if (head_maps) { B200_ATTN_LAUNCH(true, false) } else { B200_ATTN_LAUNCH(false, false) }
+  }
+#undef B200_ATTN_LAUNCH
   if (lr != B200_OK) return lr;
   if (int r = check_launch("paged_attn_fwd_kernel")) return r;
 
@@ -576,8 +582,9 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   if (splits <= 4) b200::unit_combine_kernel<T, D, 4><<<cgrid, b200::kCombineThreads, 0, s>>>(c);               \
   else if (splits <= 8) b200::unit_combine_kernel<T, D, 8><<<cgrid, b200::kCombineThreads, 0, s>>>(c);          \
   else b200::unit_combine_kernel<T, D, 16><<<cgrid, b200::kCombineThreads, 0, s>>>(c);
-#define B200_UCOMB_D(T)                                 \
-  if (p->head_dim == 64) { B200_UCOMB_S(T, 64) } else { B200_UCOMB_S(T, 128) }
+#define B200_UCOMB_D(T)                                                                          \
+  if (p->head_dim == 64) { B200_UCOMB_S(T, 64) } else if (p->head_dim == 128) { B200_UCOMB_S(T, 128) } \
+  else { B200_UCOMB_S(T, 256) }
     if (bf16) { B200_UCOMB_D(__nv_bfloat16) } else { B200_UCOMB_D(__half) }
 #undef B200_UCOMB_D
 #undef B200_UCOMB_S

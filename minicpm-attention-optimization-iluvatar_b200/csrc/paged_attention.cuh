@@ -246,11 +246,20 @@ __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
   }
 }
 
-template <typename T, bool kHeadMaps>
+// kWide: head_dim 256.  A unit is then one query tile (TMEM: S 128 columns +
+// O 256 columns, where the narrow kernel holds two S and two O), Q fills the
+// whole 64 KB Q area (four 64-column quarters), and every KV tile takes four
+// ring slots -- K and V each as two 128-column halves, each half in the narrow
+// kernel's slot layout -- so S = Q K^T is 16 UMMAs over two K slots and
+// O += P V two N = 128 UMMA chains, one per V half.  The second softmax
+// warpgroup has no tile and idles.
+template <typename T, bool kHeadMaps, bool kWide>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     paged_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ KvHeadMaps maps,
                           const AttnKernelArgs a) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int kTilesPerUnit = kWide ? 1 : kAttnTilesPerUnit;
+  constexpr int kFillsPerTile = kWide ? 4 : 2;  // ring slots per KV tile: K (, K hi), V (, V hi)
   griddep_wait();  // launched as a programmatic dependent of the schedule kernel
 
   extern __shared__ uint8_t smem_raw[];
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int P = a.pos_per_tile;
-  const int ppu = kAttnTilesPerUnit * P;
+  const int ppu = kTilesPerUnit * P;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(BAR_Q_FULL), 1);
@@ -380,18 +389,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const UnitGeom ug = geometry(e);
         const int n_tiles = ug.n_tiles;
         if (n_tiles == 0) continue;
-        const bool two = ug.pos0 + P < ug.q_len;
+        const bool two = !kWide && ug.pos0 + P < ug.q_len;
         if (lane == 0) {
           ok = mbar_wait(bar(BAR_Q_EMPTY), (q_loads & 1) ^ 1, abort_flag);
           if (ok) {
             const int head0 = e.kvh * a.group;
             const int t0 = ug.q_begin + ug.pos0;
-            mbar_arrive_expect_tx(bar(BAR_Q_FULL), (two ? 2 : 1) * q_rows * 256);  // 2 halves of 128 B rows
-            tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q_FULL), 0, head0, t0);
-            tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q_FULL), 64, head0, t0);
-            if (two) {
-              tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q_FULL), 0, head0, t0 + P);
-              tma_load_3d(sbase + kSmQ + 49152, &tm_q, bar(BAR_Q_FULL), 64, head0, t0 + P);
+            if (kWide) {  // one tile, four 64-column quarters of 128 B rows
+              mbar_arrive_expect_tx(bar(BAR_Q_FULL), 4 * q_rows * 128);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+                tma_load_3d(sbase + kSmQ + q4 * 16384, &tm_q, bar(BAR_Q_FULL), 64 * q4, head0, t0);
+            } else {
+              mbar_arrive_expect_tx(bar(BAR_Q_FULL), (two ? 2 : 1) * q_rows * 256);  // 2 halves of 128 B rows
+              tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q_FULL), 0, head0, t0);
+              tma_load_3d(sbase + kSmQ + 16384, &tm_q, bar(BAR_Q_FULL), 64, head0, t0);
+              if (two) {
+                tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q_FULL), 0, head0, t0 + P);
+                tma_load_3d(sbase + kSmQ + 49152, &tm_q, bar(BAR_Q_FULL), 64, head0, t0 + P);
+              }
             }
           }
         }
@@ -410,12 +426,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         lookup(0, pg_cur, of_cur);
         if (n_tiles > 1) lookup(1, pg_nxt, of_nxt);
         bool stop = false;
-        for (int idx = 0; idx < 2 * n_tiles; ++idx) {
-          const int j = idx >> 1;
-          const bool is_v = idx & 1;
+        for (int idx = 0; idx < kFillsPerTile * n_tiles; ++idx) {
+          const int j = idx / kFillsPerTile;
+          const int part = idx % kFillsPerTile;  // K, V  or  K lo, K hi, V lo, V hi
+          const bool is_v = part >= kFillsPerTile / 2;
+          const int hi = kWide ? (part & 1) : 0;  // 128-column half of a head_dim-256 row
           const int slot = issued % kKvStages;
           const uint32_t ph = (issued / kKvStages) & 1;
-          if (!is_v && j > 0) {
+          if (part == 0 && j > 0) {
             pg_cur = pg_nxt;
             of_cur = of_nxt;
             if (j + 1 < n_tiles) lookup(j + 1, pg_nxt, of_nxt);
@@ -436,14 +454,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // lane c < 8 issues slice c (its own lookup): 16 keys x both halves.
             if (lane < 8) {
               const CUtensorMap* map = is_v ? &maps.v[e.kvh] : &maps.k[e.kvh];
-              tma_load_5d(sbase + kSmKV + slot * 32768 + lane * 4096, map, bar(BAR_KV_FULL + slot), 0, 0, 0,
+              tma_load_5d(sbase + kSmKV + slot * 32768 + lane * 4096, map, bar(BAR_KV_FULL + slot), 0, 0, 2 * hi,
                           off >> 3, page);
             }
           } else if (lane < 16) {
             const int half = lane & 1;
             const CUtensorMap* map = is_v ? &maps.v[0] : &maps.k[0];
             tma_load_4d(sbase + kSmKV + slot * 32768 + half * 16384 + c * 2048, map, bar(BAR_KV_FULL + slot),
-                        half * 64, off, e.kvh, page);
+                        half * 64 + hi * 128, off, e.kvh, page);
           }
           ++issued;
         }
@@ -504,7 +522,76 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       auto wait_full = [&](int g) {
         return mbar_wait(bar(BAR_KV_FULL + g % kKvStages), (g / kKvStages) & 1, abort_flag);
       };
-      for (int it = 0;; ++it) {
+      // head_dim 256: S over the four Q quarters and two K slots; O lo / hi
+      // (TMEM columns 256 / 384) from the two V slots, both with P of S0.
+      auto issue_s_wide = [&](uint32_t klo, uint32_t khi) {
+        const uint64_t qd = umma_desc_sw128(sbase + kSmQ, 16, 1024);
+        const uint64_t kdl = umma_desc_sw128(klo, 16, kHeadMaps ? 2048 : 1024);
+        const uint64_t kdh = umma_desc_sw128(khi, 16, kHeadMaps ? 2048 : 1024);
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          const uint32_t qoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint32_t koff = kv_slot_offset<kHeadMaps>(0, (kk >> 2) & 1, 0) + (kk & 3) * 32;
+          umma_ss(tmem, qd + (qoff >> 4), (kk < 8 ? kdl : kdh) + (koff >> 4), idesc_qk, kk > 0);
+        }
+        tc_commit(bar(BAR_S_FULL));
+      };
+      auto issue_pv_wide = [&](int c, uint32_t vlo, uint32_t vhi, bool acc, bool last) {
+        const uint64_t vdl = umma_desc_sw128(vlo, kHeadMaps ? 1024 : 16384, kHeadMaps ? 2048 : 1024);
+        const uint64_t vdh = umma_desc_sw128(vhi, kHeadMaps ? 1024 : 16384, kHeadMaps ? 2048 : 1024);
+        for (int q = 0; q < 4; ++q) {
+          if (q % 2 == 0) {
+            if (!mbar_wait(bar(BAR_P_FULL + q / 2), c & 1, abort_flag)) return false;
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int kk = 2 * q + h;
+            const uint32_t voff = kv_slot_offset<kHeadMaps>(16 * kk, 0, 0) >> 4;
+            umma_ts(tmem + 256, tmem + kk * 8, vdl + voff, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+            umma_ts(tmem + 384, tmem + kk * 8, vdh + voff, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          }
+        }
+        if (last) tc_commit(bar(BAR_O_DONE));
+        return true;
+      };
+      for (int it = 0; kWide; ++it) {
+        // head_dim 256, one query tile per unit: S(j), PV(j), S(j + 1), ...
+        // (S(j + 1) overwrites the S columns that hold P(j) only after PV(j)
+        // has read them: the tensor core runs them in issue order).
+        UnitEntry e;
+        if (!take_entry(it, e)) break;
+        mbar_arrive(bar(BAR_IT_EMPTY + it % kUnitRing));
+        if (!e.valid) break;
+        const UnitGeom ug = geometry(e);
+        const int n_tiles = ug.n_tiles;
+        if (n_tiles == 0) continue;
+        bool ok = mbar_wait(bar(BAR_Q_FULL), q_uses & 1, abort_flag);
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int f = fills + 4 * j;
+          if (!wait_full(f) || !wait_full(f + 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s_wide(slot_addr(f), slot_addr(f + 1));
+          if (j + 1 == n_tiles) tc_commit(bar(BAR_Q_EMPTY));  // the unit's last S is issued
+          tc_commit(bar(BAR_KV_EMPTY + f % kKvStages));
+          tc_commit(bar(BAR_KV_EMPTY + (f + 1) % kKvStages));
+          if (!wait_full(f + 2) || !wait_full(f + 3) ||
+              !issue_pv_wide(tiles_done[0] + j, slot_addr(f + 2), slot_addr(f + 3), j > 0, j + 1 == n_tiles)) {
+            ok = false;
+            break;
+          }
+          tc_commit(bar(BAR_KV_EMPTY + (f + 2) % kKvStages));
+          tc_commit(bar(BAR_KV_EMPTY + (f + 3) % kKvStages));
+        }
+        if (!ok) break;
+        fills += 4 * n_tiles;
+        ++q_uses;
+        tiles_done[0] += n_tiles;
+      }
+      for (int it = 0; !kWide; ++it) {
         UnitEntry e;
         if (!take_entry(it, e)) break;
         mbar_arrive(bar(BAR_IT_EMPTY + it % kUnitRing));
@@ -579,9 +666,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!e.valid) break;
       const UnitGeom ug = geometry(e);
       const int n_tiles = ug.n_tiles;
-      const bool two = ug.pos0 + P < ug.q_len;
+      const bool two = !kWide && ug.pos0 + P < ug.q_len;
       const int unit_fills = fills;
-      fills += 2 * n_tiles;
+      fills += kFillsPerTile * n_tiles;
       if (!(t == 0 || two)) continue;
       const int tile_pos0 = ug.pos0 + t * P;
       const int row_pos = tile_pos0 + row / a.group;
@@ -686,7 +773,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // S_FULL phase of tile j already implies PV_{j-1} is complete: its
             // commit covers every UMMA the issuer started before S_j.
 #pragma unroll 1
-            for (int c8 = 0; c8 < 8; ++c8) {
+            for (int c8 = 0; c8 < (kWide ? 16 : 8); ++c8) {  // O, 16 columns at a time
               uint32_t o[16];
               tmem_ld16(o_addr + 16 * c8, o);
               tmem_wait_ld16(o);
@@ -706,17 +793,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           // Rows of the last page past the sequence end may hold anything (NaN
           // included); P is 0 there but 0 * NaN is NaN, so zero those V rows,
           // as the reference's masked V load does (triton_split_kv_paged.py:122).
-          const int vidx = unit_fills + 2 * j + 1;
-          if (!mbar_wait(bar(BAR_KV_FULL + vidx % kKvStages), (vidx / kKvStages) & 1, abort_flag)) {
+          bool landed = true;
+          for (int vs = 0; vs < (kWide ? 2 : 1) && landed; ++vs) {  // the V slot(s) of the last tile
+            const int vidx = unit_fills + kFillsPerTile * j + kFillsPerTile / 2 + vs;
+            if (!mbar_wait(bar(BAR_KV_FULL + vidx % kKvStages), (vidx / kKvStages) & 1, abort_flag)) {
+              landed = false;
+              break;
+            }
+            const uint32_t vbase = sbase + kSmKV + (vidx % kKvStages) * 32768;
+            const int n16 = (v_tail_to - v_tail_from) * 16;  // 16-byte pieces over both halves
+            for (int i = threadIdx.x - 128; i < n16; i += 128) {
+              const int r = v_tail_from + (i >> 4);
+              const int half = (i >> 3) & 1;
+              st_shared_v4(vbase + kv_slot_offset<kHeadMaps>(r, half, i & 7), 0u, 0u, 0u, 0u);
+            }
+          }
+          if (!landed) {
             aborted = true;
             break;
-          }
-          const uint32_t vbase = sbase + kSmKV + (vidx % kKvStages) * 32768;
-          const int n16 = (v_tail_to - v_tail_from) * 16;  // 16-byte pieces over both halves
-          for (int i = threadIdx.x - 128; i < n16; i += 128) {
-            const int r = v_tail_from + (i >> 4);
-            const int half = (i >> 3) & 1;
-            st_shared_v4(vbase + kv_slot_offset<kHeadMaps>(r, half, i & 7), 0u, 0u, 0u, 0u);
           }
           fence_proxy_async_smem();
         }
@@ -773,7 +867,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c4 = 0; c4 < (kWide ? 8 : 4); ++c4) {
         if (c4 * 32 >= a.head_dim) break;  // warp-uniform: only the row's real columns
         uint32_t o[32];
         if (n_tiles > 0) {

@@ -11,7 +11,8 @@ same signature, same feature guards, same routing, same exceptions.
   window, ``q_descale``, sinks, ``use_td``); failures on that path propagate,
   there is no silent fallback (``kernels/attention.py:151-152``).
 * A head shape or element type the sm_100a kernel does not run (fp32,
-  head_dim 256, more than 128 query heads per KV head; ``kernel_supports``)
+  head_dim other than 64 / 128 / 256, more than 128 query heads per KV head;
+  ``kernel_supports``)
   is routed like an unsupported feature: the reference's Triton kernel took
   these shapes, so they must not turn into an error here.
 * Otherwise the call goes to vLLM's ``unified_attention``, as in the

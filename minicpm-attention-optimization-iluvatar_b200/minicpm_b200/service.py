@@ -9,8 +9,8 @@ reference's integration patch adds it (``integration/vllm-plugin-FL-split-kv.pat
   no unsupported feature (KV quantisation, ALiBi, sinks, softcap, a sliding
   window, any descale, tensor descriptors, non-causal), else vLLM's
   ``unified_attention``.  A head shape or dtype the sm_100a kernel does not
-  run (``kernel_supports``: fp32, head_dim 256, more than 128 query heads per
-  KV head) takes the vLLM route too.  Pure decode (``max_seqlen_q <= 1``) stays on vLLM
+  run (``kernel_supports``: fp32, head_dim other than 64 / 128 / 256, more than
+  128 query heads per KV head) takes the vLLM route too.  Pure decode (``max_seqlen_q <= 1``) stays on vLLM
   unless ``ILUVATAR_SPLIT_KV_DECODE`` is also set, which selects the sm_100a
   decode kernel (the reference kept decode on vLLM).  Failures of the sm_100a
   path propagate; there is no silent fallback.

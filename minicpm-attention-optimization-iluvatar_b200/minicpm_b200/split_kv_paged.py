@@ -156,9 +156,9 @@ def kernel_supports(q: torch.Tensor, k: torch.Tensor) -> bool:
 
     ``q`` is ``[T, Hq, D]``; ``k`` is the 4-D ``[blocks, block, KH, D]`` cache
     or the 5-D ``[blocks, 2, block, KH, D]`` one.  The dispatcher and the
-    service route calls for which this is false (fp32, head_dim 256, more than
-    128 query heads per KV head) to their baseline kernel, as they route the
-    features the kernel does not implement.
+    service route calls for which this is false (fp32, head_dim other than
+    64 / 128 / 256, more than 128 query heads per KV head) to their baseline
+    kernel, as they route the features the kernel does not implement.
     """
     try:
         code = _lib.dtype_code(q.dtype)

@@ -217,7 +217,8 @@ def test_dispatcher_unsupported_features_go_to_vllm(routes, monkeypatch, over):
 
 
 @pytest.mark.parametrize("hq,hkv,d,dtype,optimized_route", [
-    (16, 2, 256, torch.bfloat16, False), (16, 2, 128, torch.float32, False), (256, 1, 128, torch.bfloat16, False),
+    (16, 2, 256, torch.bfloat16, True), (16, 2, 96, torch.bfloat16, False), (16, 2, 128, torch.float32, False),
+    (256, 1, 128, torch.bfloat16, False),
     (12, 2, 128, torch.bfloat16, True), (16, 2, 64, torch.float16, True)])
 def test_dispatcher_routes_shapes_the_kernel_does_not_run_to_vllm(routes, monkeypatch, hq, hkv, d, dtype,
                                                                   optimized_route):

@@ -338,3 +338,43 @@ def test_head_dim_64_decode_batch_and_dispatcher(monkeypatch):
     cpu = small_batch([20, 33], [100, 400], seed=66, head_dim=64)
     assert_close(out.cpu(), oracle(cpu), "d64 dispatcher")
     _no_device_error()
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 2), (8, 8), (16, 1), (12, 2)])
+def test_head_dim_256_against_oracle(hq, hkv):
+    """head_dim 256 (accepted by the reference wrapper,
+    kernels/triton_split_kv_paged.py:270): the kernel's wide variant, one
+    query tile per unit, K and V in two 128-column halves; partial pages, a
+    decode row, splits 1 / 4 / auto and every unit split 4 ways."""
+    batch = small_batch([37, 1, 100, 16, 300], [200, 63, 1000, 0, 2500], seed=256, num_q_heads=hq, num_kv_heads=hkv,
+                        head_dim=256)
+    want = oracle(batch)
+    for s in (1, 4, 0):
+        assert_close(run_gpu(batch, s), want, f"d256 {hq}/{hkv} S={s}")
+    with pytest.MonkeyPatch.context() as mp:
+        mp.setenv("B200_ATTN_SPLIT_UNIFORM", "1")
+        assert_close(run_gpu(batch, 4), want, f"d256 {hq}/{hkv} uniform S=4")
+    _no_device_error()
+
+
+def test_head_dim_256_chunked_prefill_and_dispatcher(monkeypatch):
+    """head_dim 256 on 8 sequences of the 4K config (sampled rows of every
+    sequence against the oracle), fp16, decode rows, and a call through the
+    dispatcher with the 5-D cache."""
+    q, kv = lengths_chunked_4k(num_seqs=8)
+    batch = build_attention_batch(q, kv, head_dim=256)
+    want, rows = sampled_oracle(batch, sample_blocks(q))
+    assert_close(run_gpu(batch, 0)[rows], want, "d256 4k")
+    half = small_batch([40, 3], [200, 77], seed=257, head_dim=256, dtype=torch.float16)
+    assert_close(run_gpu(half, 1), oracle(half), "d256 fp16")
+    dec = small_batch([1, 1, 1], [5, 700, 2048], seed=258, head_dim=256)
+    assert_close(run_gpu(dec, 0), oracle(dec), "d256 decode rows")
+    b = small_batch([20, 33], [100, 400], seed=259, head_dim=256).to("cuda")
+    out = torch.empty_like(b.q)
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    iluvatar_attention(b.q, b.kv_cache, b.kv_cache, out, b.cu_seqlens_q, b.max_seqlen_q, b.seqused_k, b.max_seqlen_k,
+                       b.softmax_scale, causal=True, block_table=b.block_table)
+    torch.cuda.synchronize()
+    assert_close(out.cpu(), oracle(small_batch([20, 33], [100, 400], seed=259, head_dim=256)), "d256 dispatcher")
+    _no_device_error()

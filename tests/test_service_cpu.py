@@ -86,7 +86,8 @@ def test_unsupported_features_and_decode_stay_on_vllm(routes, monkeypatch, over)
 @pytest.mark.parametrize(
     "shape,route",
     [
-        (dict(d=256), "vllm"),  # head_dim 256: the reference's Triton kernel took it, the sm_100a kernel does not
+        (dict(d=256), "b200"),  # head_dim 256: the kernel's wide variant
+        (dict(d=96), "vllm"),  # a head size the sm_100a kernel does not run
         (dict(hq=12, hkv=2), "b200"),  # GQA 6:1 (128 rows hold 21 positions x 6 heads)
         (dict(hq=24, hkv=2), "b200"),  # GQA 12:1
         (dict(hq=256, hkv=1), "vllm"),  # more than 128 query heads per KV head

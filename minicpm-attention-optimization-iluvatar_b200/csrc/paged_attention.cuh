@@ -1166,8 +1166,9 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
 // per D/8 threads, over a grid-stride loop whose bound (the split-unit count)
 // the schedule kernel left on the device; a call without split units costs
 // one launch that exits at once.  Row r of a unit is query tile r / 128, tile
-// row r % 128 = (position, head) as in the attention kernel; padding rows and
-// positions past the sequence's query rows are skipped.
+// row r % 128 = (position, head) as in the attention kernel; padding rows,
+// tiles the unit does not have and positions past the sequence's query rows
+// are skipped.
 // ---------------------------------------------------------------------------
 struct UnitCombineArgs {
   const void* o_part;      // [slots][num_splits][kUnitRows][head_dim], query dtype
@@ -1202,7 +1203,9 @@ __global__ void __launch_bounds__(kCombineThreads) unit_combine_kernel(const Uni
     const int q_begin = load_index(a.cu_q, su.x, a.len_i64);
     const int q_len = load_index(a.cu_q, su.x + 1, a.len_i64) - q_begin;
     const int pos = su.y * a.pos_per_unit + t * a.pos_per_tile + r / a.group;
-    const bool valid = in_range && r < a.group * a.pos_per_tile && pos < q_len;
+    // Rows of a tile the unit does not have (the second tile of a head_dim-256
+    // unit, which holds one) would name the next unit's positions: skipped.
+    const bool valid = in_range && r < a.group * a.pos_per_tile && t * a.pos_per_tile < a.pos_per_unit && pos < q_len;
     const int64_t prow = static_cast<int64_t>(slot) * a.num_splits * kUnitRows + ur;
     const int64_t tok = q_begin + pos, head = static_cast<int64_t>(su.z) * a.group + r % a.group;
     combine_row<T, T, D, kS>(static_cast<const T*>(a.o_part) + prow * D, static_cast<int64_t>(kUnitRows) * D,

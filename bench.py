@@ -46,6 +46,7 @@ for _p in (str(ROOT), str(PKG_DIR)):
 import torch  # noqa: E402
 
 METRIC = "paged prefill attention TFLOP/s & tokens/s at 4K/16K ctx, 64 seqs, 1/2/4/8 B200; % TC peak"
+HEAD_DIM = 128  # attention workloads; --head-dim 64 / 256 measures the other head sizes on the same shapes
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
@@ -59,6 +60,8 @@ def parse_args():
                     choices=["chunked_prefill_16k", "chunked_prefill_4k", "mixed_256", "decode_16k", "decode_4k",
                              "rope_16384", "kv_write_16384", "split_combine_4k"])
     ap.add_argument("--splits", type=int, default=0, help="0 = automatic")
+    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128, 256],
+                    help="attention workloads: head size (the headline is 128)")
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="keep only the first N sequences of the workload (small cases for profiling)")
     ap.add_argument("--rotary-dim", type=int, default=128)
@@ -211,8 +214,8 @@ def build_local_batch(workload: str, world: int, rank: int, num_seqs: int = 0):
     q, kv = workloads.WORKLOADS[workload]()
     if num_seqs:
         q, kv = q[:num_seqs], kv[:num_seqs]
-    ids = lpt_shard(q, kv, world, 16, 128)[rank]
-    batch = workloads.build_attention_batch([q[i] for i in ids], [kv[i] for i in ids], seq_ids=ids)
+    ids = lpt_shard(q, kv, world, 16, HEAD_DIM)[rank]
+    batch = workloads.build_attention_batch([q[i] for i in ids], [kv[i] for i in ids], seq_ids=ids, head_dim=HEAD_DIM)
     return batch, q, kv
 
 
@@ -229,7 +232,7 @@ def cpu_sample_flops(batch, rows: int):
                          cu_seqlens_q=torch.tensor([0, r1 - r0], dtype=torch.int32),
                          seqused_k=torch.tensor([L], dtype=torch.int32), query_lens=[r1 - r0], kv_lens=[L],
                          softmax_scale=batch.softmax_scale, seq_ids=batch.seq_ids[:1])
-    flops = causal_flops([r1 - r0], [L], 16, 128)
+    flops = causal_flops([r1 - r0], [L], 16, HEAD_DIM)
 
     def run():
         paged_attention_reference(sub.q, sub.k_cache, sub.v_cache, sub.block_table, sub.cu_seqlens_q, sub.seqused_k,
@@ -266,16 +269,16 @@ def attention_config(workload: str, world: int, splits: int, num_seqs: int = 0) 
         from minicpm_b200.sharding import lpt_shard
 
         # rank 0's shard decides the automatic count the call resolves to
-        ids = lpt_shard(q, kv, world, 16, 128)[0]
+        ids = lpt_shard(q, kv, world, 16, HEAD_DIM)[0]
         resolved = choose_num_splits(sum(q[i] for i in ids), len(ids), 16, 2, max(kv[i] for i in ids))
-    kv_mb = sum(workloads.attention_kv_bytes([0], [L]) for L in kv) / 1e6 / world
-    q_mb = sum(q) * 16 * 128 * 2 / 1e6 / world
+    kv_mb = sum(workloads.attention_kv_bytes([0], [L], head_dim=HEAD_DIM) for L in kv) / 1e6 / world
+    q_mb = sum(q) * 16 * HEAD_DIM * 2 / 1e6 / world
     return {
         "workload": workload,
         "seqs": len(q),
         "query_tokens": sum(q),
-        "causal_flops": float(causal_flops(q, kv, 16, 128)),
-        "heads": "16q/2kv", "head_dim": 128, "page_size": 16,
+        "causal_flops": float(causal_flops(q, kv, 16, HEAD_DIM)),
+        "heads": "16q/2kv", "head_dim": HEAD_DIM, "page_size": 16,
         "num_splits": resolved,
         "parallelism": f"sequence-sharded x{world} (LPT by causal FLOPs)",
         "l2": "inputs larger than L2 (KV %.0f MB + Q %.0f MB per GPU)" % (kv_mb, q_mb),
@@ -300,7 +303,7 @@ def reference_arm(args, world, rank):
     from minicpm_b200 import workloads
 
     q, kv = workloads.WORKLOADS[args.workload]()
-    batch = workloads.build_attention_batch(q[:1], kv[:1], seq_ids=[0])
+    batch = workloads.build_attention_batch(q[:1], kv[:1], seq_ids=[0], head_dim=HEAD_DIM)
     run, flops, desc = cpu_sample_flops(batch, 512)
     for _ in range(args.warmup):
         run()
@@ -625,7 +628,8 @@ def verify_sharded(args, batch, out, world, rank, splits):
     q, kv = workloads.WORKLOADS[args.workload]()
     if args.num_seqs:
         q, kv = q[: args.num_seqs], kv[: args.num_seqs]
-    ref = workloads.build_attention_batch([q[i] for i in order], [kv[i] for i in order], seq_ids=order).to(full.device)
+    ref = workloads.build_attention_batch([q[i] for i in order], [kv[i] for i in order], seq_ids=order,
+                                          head_dim=HEAD_DIM).to(full.device)
     want = torch.empty_like(ref.q)
     paged_split_kv_attention(ref.q, ref.kv_cache[:, 0], ref.kv_cache[:, 1], want, ref.block_table, ref.seqused_k,
                              ref.cu_seqlens_q, ref.max_seqlen_q, ref.max_seqlen_k, ref.softmax_scale, num_splits=splits)
@@ -791,8 +795,8 @@ def attention_run(workload: str, splits: int, steps: int, warmup: int, world: in
 
     dev = torch.device("cuda", local)
     batch, all_q, all_kv = build_local_batch(workload, world, rank, num_seqs)
-    local_flops = causal_flops(batch.query_lens, batch.kv_lens, 16, 128)
-    local_bytes = attention_kv_bytes(batch.query_lens, batch.kv_lens)
+    local_flops = causal_flops(batch.query_lens, batch.kv_lens, 16, HEAD_DIM)
+    local_bytes = attention_kv_bytes(batch.query_lens, batch.kv_lens, head_dim=HEAD_DIM)
     total_bytes = sum_over_ranks(float(local_bytes), world)
     total_flops = sum_over_ranks(float(local_flops), world)
     g = batch.to(dev)
@@ -958,7 +962,7 @@ def attention_bench(args, world, rank, local):
         verify_sharded(args, batch, out, world, rank, args.splits)
 
     subs = None
-    if args.workload == "chunked_prefill_16k" and not args.no_sub and not args.num_seqs:
+    if args.workload == "chunked_prefill_16k" and not args.no_sub and not args.num_seqs and HEAD_DIM == 128:
         del r["g"], r["out"]
         out = None
         torch.cuda.empty_cache()
@@ -1035,7 +1039,9 @@ def attention_bench(args, world, rank, local):
 
 
 def main():
+    global HEAD_DIM
     args = parse_args()
+    HEAD_DIM = args.head_dim
     if args.impl == "reference":
         # Rank 0 alone times the host-core implementation; other ranks exit at once.
         if int(os.environ.get("RANK", "0")) == 0:

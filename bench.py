@@ -82,10 +82,31 @@ def parse_args():
 
 
 # --------------------------------------------------------------------- ranks
+def pin_to_gpu_numa_node(local: int) -> None:
+    """Run this rank on the host cores next to its GPU (the PCI device's
+    ``local_cpulist``), so the pinned host buffers of the e2e copies are
+    first-touched on that NUMA node; a no-op where sysfs does not say."""
+    try:
+        prop = torch.cuda.get_device_properties(local)
+        bdf = f"{prop.pci_domain_id:04x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+        text = Path(f"/sys/bus/pci/devices/{bdf}/local_cpulist").read_text().strip()
+        cpus = set()
+        for part in text.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+    except Exception:
+        pass
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        pin_to_gpu_numa_node(local)
     if world > 1:
         import datetime
 

@@ -300,6 +300,54 @@ typedef struct B200KvWriteParams {
 
 B200_API int b200_kv_cache_write(const B200KvWriteParams* params, void* stream);
 
+/*
+ * Dequantise the pages a batch references, for attention over a quantised KV
+ * cache (the service's fp8 / int8 caches; the reference sends those calls to
+ * vLLM's unified_attention, integration/vllm-plugin-FL-split-kv.patch:473-523).
+ * For sequence b and page p < ceil(seqused_k[b] / block_size), the cache rows
+ * of block_table[b, p] go to dense page b * max_pages + p of out_cache
+ * [num_seqs * max_pages, 2 (K, V), block_size, num_kv_heads, head_dim] in
+ * out_dtype, and out_block_table[b, p] = b * max_pages + p for every p <
+ * max_pages; b200_paged_attn_fwd then runs on out_cache[:, 0] / [:, 1] with
+ * out_block_table.  Element values: FP8_PER_TENSOR fp8(x) * *k_scale (resp.
+ * *v_scale); *_PER_TOKEN_HEAD x * scale_cache[block, slot, head]; both rounded
+ * to nearest in out_dtype.  Cache element types: FP8_E4M3 / FP8_E5M2
+ * (per-tensor), I8 / FP8_E4M3 (per-token-head).  Cache strides in elements
+ * (bytes), multiples of 4; head_dim a multiple of 4.  A block id outside
+ * [0, num_blocks) gives a zero page.
+ */
+typedef struct B200KvDequantParams {
+  const void* key_cache;
+  const void* value_cache;
+  int64_t kc_stride_block, kc_stride_tok, kc_stride_head;
+  int64_t vc_stride_block, vc_stride_tok, vc_stride_head;
+  const float* k_scale;        /* FP8_PER_TENSOR */
+  const float* v_scale;
+  const float* k_scale_cache;  /* *_PER_TOKEN_HEAD, float element strides below */
+  const float* v_scale_cache;
+  int64_t ks_stride_block, ks_stride_tok, ks_stride_head;
+  int64_t vs_stride_block, vs_stride_tok, vs_stride_head;
+  const void* block_table;
+  int64_t block_table_stride;
+  int32_t block_table_cols;
+  int32_t block_table_dtype; /* I32 / I64 */
+  const void* seqused_k;
+  int32_t seqlen_dtype;      /* I32 / I64 */
+  void* out_cache;
+  int32_t* out_block_table;  /* [num_seqs, max_pages] */
+  int32_t num_seqs;
+  int32_t max_pages;
+  int32_t block_size;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t num_blocks;
+  int32_t cache_dtype;       /* FP8_E4M3 / FP8_E5M2 / I8 */
+  int32_t quant_mode;        /* B200_KVQ_FP8_PER_TENSOR / _INT8_PER_TOKEN_HEAD / _FP8_PER_TOKEN_HEAD */
+  int32_t out_dtype;         /* BF16 / F16 */
+} B200KvDequantParams;
+
+B200_API int b200_kv_dequant_pages(const B200KvDequantParams* params, void* stream);
+
 /* Message of the last failed call on this host thread ("" if none). */
 B200_API const char* b200_last_error(void);
 

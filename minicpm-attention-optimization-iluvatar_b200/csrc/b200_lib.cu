@@ -25,6 +25,7 @@
 #include "rope_kv_cache.cuh"
 #include "split_combine.cuh"
 #include "kv_cache_write.cuh"
+#include "kv_dequant.cuh"
 
 namespace {
 
@@ -829,6 +830,68 @@ int b200_kv_cache_write(const B200KvWriteParams* p, void* stream) {
 #undef B200_KV_MODES
 #undef B200_KV_CPR
   return check_launch("kv_cache_write_kernel");
+}
+
+int b200_kv_dequant_pages(const B200KvDequantParams* p, void* stream) {
+  if (!p) return fail(B200_ERR_INVALID, "null params");
+  const bool per_tensor = p->quant_mode == B200_KVQ_FP8_PER_TENSOR;
+  const bool per_token_head =
+      p->quant_mode == B200_KVQ_INT8_PER_TOKEN_HEAD || p->quant_mode == B200_KVQ_FP8_PER_TOKEN_HEAD;
+  if (!per_tensor && !per_token_head)
+    return fail(B200_ERR_UNSUPPORTED, "KV quantisation mode %d has no dequantisation here", p->quant_mode);
+  if (per_tensor && p->cache_dtype != B200_DTYPE_FP8_E4M3 && p->cache_dtype != B200_DTYPE_FP8_E5M2)
+    return fail(B200_ERR_INVALID, "fp8 per-tensor caches must be float8 e4m3 or e5m2");
+  if (p->quant_mode == B200_KVQ_INT8_PER_TOKEN_HEAD && p->cache_dtype != B200_DTYPE_I8)
+    return fail(B200_ERR_INVALID, "int8 per-token-head caches must be int8");
+  if (p->quant_mode == B200_KVQ_FP8_PER_TOKEN_HEAD && p->cache_dtype != B200_DTYPE_FP8_E4M3)
+    return fail(B200_ERR_INVALID, "fp8 per-token-head caches must be float8 e4m3");
+  if (per_tensor && (!p->k_scale || !p->v_scale)) return fail(B200_ERR_INVALID, "fp8 per-tensor caches need k_scale and v_scale");
+  if (per_token_head && (!p->k_scale_cache || !p->v_scale_cache))
+    return fail(B200_ERR_INVALID, "per-token-head caches need k_scale_cache and v_scale_cache");
+  if (p->out_dtype != B200_DTYPE_BF16 && p->out_dtype != B200_DTYPE_F16)
+    return fail(B200_ERR_INVALID, "the dequantised cache must be bf16 or f16");
+  if (p->block_table_dtype != B200_DTYPE_I32 && p->block_table_dtype != B200_DTYPE_I64)
+    return fail(B200_ERR_INVALID, "block_table must contain integer physical block ids");
+  if (p->seqlen_dtype != B200_DTYPE_I32 && p->seqlen_dtype != B200_DTYPE_I64)
+    return fail(B200_ERR_INVALID, "seqused_k must be int32 or int64");
+  if (p->num_seqs < 0 || p->max_pages < 0 || p->block_size <= 0 || p->num_kv_heads <= 0 || p->head_dim <= 0 ||
+      p->head_dim % 4 || p->num_blocks < 0)
+    return fail(B200_ERR_INVALID, "bad sizes");
+  if (((reinterpret_cast<uintptr_t>(p->key_cache) | reinterpret_cast<uintptr_t>(p->value_cache)) & 3) ||
+      ((p->kc_stride_block | p->kc_stride_tok | p->kc_stride_head | p->vc_stride_block | p->vc_stride_tok |
+        p->vc_stride_head) & 3))
+    return fail(B200_ERR_UNSUPPORTED, "cache rows must be 4-byte aligned");
+  if (!aligned16(p->out_cache)) return fail(B200_ERR_INVALID, "out_cache must be 16-byte aligned");
+  if (p->num_seqs == 0 || p->max_pages == 0) return B200_OK;
+  if ((int64_t)p->max_pages * p->num_seqs >= (int64_t(1) << 31) || p->num_seqs > 65535)
+    return fail(B200_ERR_UNSUPPORTED, "too many pages or sequences for one dequantisation launch");
+  b200::KvDequantArgs a{};
+  a.kc = static_cast<const uint8_t*>(p->key_cache);
+  a.vc = static_cast<const uint8_t*>(p->value_cache);
+  a.kc_sb = p->kc_stride_block; a.kc_st = p->kc_stride_tok; a.kc_sh = p->kc_stride_head;
+  a.vc_sb = p->vc_stride_block; a.vc_st = p->vc_stride_tok; a.vc_sh = p->vc_stride_head;
+  a.k_scale = p->k_scale; a.v_scale = p->v_scale; a.ksc = p->k_scale_cache; a.vsc = p->v_scale_cache;
+  a.ks_sb = p->ks_stride_block; a.ks_st = p->ks_stride_tok; a.ks_sh = p->ks_stride_head;
+  a.vs_sb = p->vs_stride_block; a.vs_st = p->vs_stride_tok; a.vs_sh = p->vs_stride_head;
+  a.block_table = p->block_table; a.bt_stride = p->block_table_stride; a.bt_cols = p->block_table_cols;
+  a.bt_i64 = p->block_table_dtype == B200_DTYPE_I64;
+  a.seqused = p->seqused_k; a.len_i64 = p->seqlen_dtype == B200_DTYPE_I64;
+  a.out = p->out_cache; a.out_table = p->out_block_table;
+  a.num_seqs = p->num_seqs; a.max_pages = p->max_pages; a.block_size = p->block_size; a.hkv = p->num_kv_heads;
+  a.head_dim = p->head_dim; a.num_blocks = p->num_blocks;
+  const dim3 grid((unsigned)p->max_pages, (unsigned)p->num_seqs);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define B200_DQ(T, ELEM, PTH) b200::kv_dequant_kernel<T, ELEM, PTH><<<grid, b200::kDequantThreads, 0, s>>>(a);
+#define B200_DQ_T(T)                                                                               \
+  if (p->quant_mode == B200_KVQ_FP8_PER_TENSOR) {                                                  \
+    if (p->cache_dtype == B200_DTYPE_FP8_E4M3) { B200_DQ(T, b200::kElemE4M3, false) }             \
+    else { B200_DQ(T, b200::kElemE5M2, false) }                                                    \
+  } else if (p->quant_mode == B200_KVQ_INT8_PER_TOKEN_HEAD) { B200_DQ(T, b200::kElemI8, true) }   \
+  else { B200_DQ(T, b200::kElemE4M3, true) }
+  if (p->out_dtype == B200_DTYPE_BF16) { B200_DQ_T(__nv_bfloat16) } else { B200_DQ_T(__half) }
+#undef B200_DQ_T
+#undef B200_DQ
+  return check_launch("kv_dequant_kernel");
 }
 
 int b200_device_error(void* stream, uint32_t* code) {

@@ -930,6 +930,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 constexpr int kSchedThreads = 1024;
 constexpr int kSchedBuckets = 2048;
 constexpr float kSchedBucketsPerOctave = 46.0f;  // 2^44 (the largest work estimate) -> bucket 2024
+constexpr int kSchedSeqCache = 4096;  // sequences whose query-unit prefix is kept in shared memory
 constexpr int kSplitBalance = 2;   // split units larger than half of one SM's share of the batch
 constexpr int kMinSplitTiles = 2;  // KV tiles each split keeps at least
 
@@ -1039,6 +1040,7 @@ __device__ __forceinline__ int qunit_splits(const SchedArgs& a, int n, long long
 __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const SchedArgs a) {
   __shared__ int hist[kSchedBuckets];
   __shared__ int warp_sums[32];
+  __shared__ int s_tile_base[kSchedSeqCache + 1];
   __shared__ int s_total_qunits;
   __shared__ unsigned long long s_total_tiles;
   griddep_launch_dependents();  // the attention grid may launch; it waits for this one
@@ -1054,25 +1056,32 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
     }
     int total;
     const int before = block_exclusive_scan(n, warp_sums, total);
-    if (b < a.num_seqs) a.tile_base[b] = carry + before;
+    if (b < a.num_seqs) {
+      a.tile_base[b] = carry + before;
+      if (b < kSchedSeqCache) s_tile_base[b] = carry + before;
+    }
     carry += total;
   }
   if (threadIdx.x == 0) {
     a.tile_base[a.num_seqs] = carry;
+    if (a.num_seqs < kSchedSeqCache) s_tile_base[a.num_seqs] = carry;
     s_total_qunits = carry;
     s_total_tiles = 0ull;
   }
   for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;
   __syncthreads();
   const int nq = s_total_qunits;
+  // The query-unit prefix, searched once per query unit: from shared memory
+  // when the batch has at most kSchedSeqCache sequences.
+  const int* tb = a.num_seqs < kSchedSeqCache ? s_tile_base : a.tile_base;
 
   // 2. KV tiles of each query unit's whole key range (kept in qunit_split for
   // now) and their sum over query units and KV heads.
   unsigned long long my_tiles = 0;
   for (int j = threadIdx.x; j < nq; j += kSchedThreads) {
-    const int seq = upper_index(a.tile_base, a.num_seqs, j);
+    const int seq = upper_index(tb, a.num_seqs, j);
     const int ql = load_index(a.cu_q, seq + 1, a.len_i64) - load_index(a.cu_q, seq, a.len_i64);
-    const int n = qunit_full_tiles(ql, load_index(a.seqused, seq, a.len_i64), j - a.tile_base[seq], a.pos_per_unit);
+    const int n = qunit_full_tiles(ql, load_index(a.seqused, seq, a.len_i64), j - tb[seq], a.pos_per_unit);
     a.qunit_split[j] = n;
     my_tiles += static_cast<unsigned long long>(n);
   }
@@ -1102,33 +1111,35 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   const int total_units = min(ucarry, a.capacity);
 
   // 4. units per work bucket; each sequence takes a contiguous range of its bucket.
-  auto seq_units = [&](int b) { return a.qunit_base[a.tile_base[b + 1]] - a.qunit_base[a.tile_base[b]]; };
+  auto seq_units = [&](int b) { return a.qunit_base[tb[b + 1]] - a.qunit_base[tb[b]]; };
   for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
-    const int qt = a.tile_base[b + 1] - a.tile_base[b];
+    const int qt = tb[b + 1] - tb[b];
     if (qt > 0) atomicAdd(&hist[seq_bucket(a, b, qt)], seq_units(b));
   }
   __syncthreads();
   buckets_to_offsets_desc(hist, warp_sums);
   __syncthreads();
   for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
-    const int qt = a.tile_base[b + 1] - a.tile_base[b];
+    const int qt = tb[b + 1] - tb[b];
     if (qt > 0) a.seq_off[b] = atomicAdd(&hist[seq_bucket(a, b, qt)], seq_units(b));
   }
   __syncthreads();
-  // 5. scatter: unit u (query unit j, then KV head, then split) goes to its
-  // sequence's range, the sequence's last query unit first.
-  for (int u = threadIdx.x; u < total_units; u += kSchedThreads) {
-    const int j = upper_index(a.qunit_base, nq, u);
-    const int seq = upper_index(a.tile_base, a.num_seqs, j);
+  // 5. scatter, one query unit per thread: its units (KV head, then split)
+  // go to its sequence's range, the sequence's last query unit first.
+  for (int j = threadIdx.x; j < nq; j += kSchedThreads) {
+    const int seq = upper_index(tb, a.num_seqs, j);
     const int s = a.qunit_split[j];
-    const int rem = u - a.qunit_base[j];
-    const int kvh = rem / s;
-    const int split = rem - kvh * s;
-    const int slot = s > 1 ? a.qunit_slot[j] * a.num_kv_heads + kvh : -1;
-    const int qunit = j - a.tile_base[seq];
-    const int pos = a.seq_off[seq] + (a.qunit_base[a.tile_base[seq + 1]] - a.qunit_base[j + 1]) + rem;
-    if (pos < a.capacity) a.units[pos] = pack_unit(seq, qunit, kvh, split, s, slot);
-    if (s > 1 && split == 0) a.split_units[slot] = make_int4(seq, qunit, kvh, s);
+    const int first = a.qunit_base[j];
+    const int qunit = j - tb[seq];
+    const int pos0 = a.seq_off[seq] + (a.qunit_base[tb[seq + 1]] - a.qunit_base[j + 1]);
+    const int slot0 = s > 1 ? a.qunit_slot[j] * a.num_kv_heads : -1;
+    for (int rem = 0; rem < s * a.num_kv_heads && first + rem < total_units; ++rem) {
+      const int kvh = rem / s;
+      const int split = rem - kvh * s;
+      const int slot = s > 1 ? slot0 + kvh : -1;
+      if (pos0 + rem < a.capacity) a.units[pos0 + rem] = pack_unit(seq, qunit, kvh, split, s, slot);
+      if (s > 1 && split == 0) a.split_units[slot] = make_int4(seq, qunit, kvh, s);
+    }
   }
   __syncthreads();
   // 6. the schedule's tail, its last kSchedThreads units, by KV-tile count

@@ -67,6 +67,7 @@ EXPORTED_SYMBOLS = (
     "b200_paged_attn_fwd_noalloc",
     "b200_rope_kv_write",
     "b200_kv_cache_write",
+    "b200_kv_dequant_pages",
     "b200_device_error",
 )
 
@@ -137,6 +138,22 @@ class KvWriteParams(ctypes.Structure):
     ]
 
 
+class KvDequantParams(ctypes.Structure):
+    _fields_ = [
+        ("key_cache", c_void_p), ("value_cache", c_void_p),
+        ("kc_stride_block", i64), ("kc_stride_tok", i64), ("kc_stride_head", i64),
+        ("vc_stride_block", i64), ("vc_stride_tok", i64), ("vc_stride_head", i64),
+        ("k_scale", c_void_p), ("v_scale", c_void_p), ("k_scale_cache", c_void_p), ("v_scale_cache", c_void_p),
+        ("ks_stride_block", i64), ("ks_stride_tok", i64), ("ks_stride_head", i64),
+        ("vs_stride_block", i64), ("vs_stride_tok", i64), ("vs_stride_head", i64),
+        ("block_table", c_void_p), ("block_table_stride", i64), ("block_table_cols", i32), ("block_table_dtype", i32),
+        ("seqused_k", c_void_p), ("seqlen_dtype", i32),
+        ("out_cache", c_void_p), ("out_block_table", c_void_p),
+        ("num_seqs", i32), ("max_pages", i32), ("block_size", i32), ("num_kv_heads", i32), ("head_dim", i32),
+        ("num_blocks", i32), ("cache_dtype", i32), ("quant_mode", i32), ("out_dtype", i32),
+    ]
+
+
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -174,6 +191,8 @@ def load() -> ctypes.CDLL:
         lib.b200_paged_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnParams), c_void_p]
         lib.b200_kv_cache_write.restype = ctypes.c_int
         lib.b200_kv_cache_write.argtypes = [ctypes.POINTER(KvWriteParams), c_void_p]
+        lib.b200_kv_dequant_pages.restype = ctypes.c_int
+        lib.b200_kv_dequant_pages.argtypes = [ctypes.POINTER(KvDequantParams), c_void_p]
         lib.b200_device_error.restype = ctypes.c_int
         lib.b200_device_error.argtypes = [c_void_p, ctypes.POINTER(ctypes.c_uint32)]
         if lib.b200_abi_version() != ABI_VERSION:

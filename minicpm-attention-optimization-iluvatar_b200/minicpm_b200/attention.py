@@ -7,9 +7,14 @@ same signature, same feature guards, same routing, same exceptions.
   unbound to ``k[:, 0]`` and ``v[:, 1]`` (``kernels/attention.py:93-96``).
 * The optimized path is taken when ``ILUVATAR_USE_OPTIMIZED=1`` and
   ``ILUVATAR_SPLIT_KV=1`` and none of the unsupported features is requested
-  (``max_seqlen_q <= 1``, softcap, KV quantisation, ALiBi, a sliding
-  window, ``q_descale``, sinks, ``use_td``); failures on that path propagate,
+  (``max_seqlen_q <= 1``, softcap, ALiBi, a sliding window, ``q_descale``,
+  sinks, ``use_td``); failures on that path propagate,
   there is no silent fallback (``kernels/attention.py:151-152``).
+* A quantised cache (``kv_quant_mode`` 1: fp8 per-tensor with
+  ``k_descale`` / ``v_descale``; 2 / 3: int8 / fp8 per-token-head with the
+  scale caches) takes the optimized path too: its referenced pages are
+  dequantised (``b200_kv_dequant_pages``) and attended by the same kernel.
+  The reference routes every quantised cache to vLLM.
 * A head shape or element type the sm_100a kernel does not run (fp32,
   head_dim other than 64 / 128 / 256, more than 128 query heads per KV head;
   ``kernel_supports``)
@@ -64,6 +69,20 @@ def _vllm_unified_attention():
     except Exception:  # vLLM missing or broken: the reference treats both as unavailable
         return None
     return unified_attention
+
+
+def _quantised_cache_supported(kv_quant_mode, k_descale, v_descale, k_scale_cache, v_scale_cache) -> bool:
+    """A quantised cache the sm_100a path dequantises: fp8 per-tensor with its
+    descales, or int8 / fp8 per-token-head with the scale caches (vLLM's
+    KVQuantMode 1 / 2 / 3)."""
+    mode = int(kv_quant_mode)
+    if mode == 0:
+        return True
+    if mode == 1:
+        return k_descale is not None and v_descale is not None
+    if mode in (2, 3):
+        return k_scale_cache is not None and v_scale_cache is not None
+    return False
 
 
 def iluvatar_attention(
@@ -122,13 +141,13 @@ def iluvatar_attention(
         or max_seqlen_q < 1
         or (max_seqlen_q == 1 and not decode_enabled())
         or softcap != 0.0
-        or kv_quant_mode != 0
+        or not _quantised_cache_supported(kv_quant_mode, k_descale, v_descale, k_scale_cache, v_scale_cache)
         or alibi_slopes is not None
         or window_size != (-1, -1)
         or q_descale is not None
         or sinks is not None
         or use_td
-        or not kernel_supports(q, k)
+        or not kernel_supports(q, k, kv_quant_mode)
     )
 
     if use_baseline:
@@ -184,6 +203,11 @@ def iluvatar_attention(
         launch_num_warps_override=launch_num_warps_override or int(os.environ.get("ILUVATAR_NUM_WARPS", "4")),
         launch_num_stages_override=launch_num_stages_override or int(os.environ.get("ILUVATAR_NUM_STAGES", "2")),
         num_splits_override=int(os.environ.get("ILUVATAR_NUM_SPLITS", "0") or 0),
+        kv_quant_mode=kv_quant_mode,
+        k_descale=k_descale,
+        v_descale=v_descale,
+        k_scale_cache=k_scale_cache,
+        v_scale_cache=v_scale_cache,
     )
 
 

@@ -289,9 +289,105 @@ def rope_and_cache(
 
 
 __all__ = [
+    "dequantize_kv_pages",
     "FP8_DTYPE",
     "is_quantized_kv_cache",
     "reshape_and_cache_flash",
     "reshape_and_cache_flash_per_token_head_quant",
     "rope_and_cache",
 ]
+
+
+# ---------------------------------------------------------------------------
+# Attention over quantised caches: the referenced pages, dequantised.
+# ---------------------------------------------------------------------------
+
+_DEQUANT_ELEM = {torch.float8_e4m3fn: _lib.DTYPE_FP8_E4M3, torch.float8_e5m2: _lib.DTYPE_FP8_E5M2,
+                 torch.int8: _lib.DTYPE_I8, torch.uint8: _lib.DTYPE_FP8_E4M3}
+
+# Dense dequantised caches cached per (device, stream): calls on one stream are
+# ordered, so they can share one buffer.
+_dense: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def dequantize_kv_pages(key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor,
+                        seqused_k: torch.Tensor, max_seqlen_k: int, kv_quant_mode: int, out_dtype: torch.dtype,
+                        head_dim: int, k_descale: torch.Tensor | None = None, v_descale: torch.Tensor | None = None,
+                        k_scale_cache: torch.Tensor | None = None, v_scale_cache: torch.Tensor | None = None
+                        ) -> tuple[torch.Tensor, torch.Tensor]:
+    """The pages ``block_table`` references, dequantised into a dense cache.
+
+    For the attention calls the reference's service makes on quantised caches
+    (``kv_quant_mode`` 1: fp8 per-tensor with ``k_descale`` / ``v_descale``,
+    whose first element is the scale, as vLLM's ``unified_attention`` reads it;
+    2 / 3: int8 / fp8 per-token-head with ``k_scale_cache`` / ``v_scale_cache``
+    ``[num_blocks, block_size, kv_heads]`` float views; the cache rows may be
+    longer than ``head_dim``, as the service's rows with the scale inline
+    are).  Returns ``(cache,
+    table)``: ``cache [num_seqs * max_pages, 2, block_size, kv_heads, head_dim]``
+    in ``out_dtype`` and ``table [num_seqs, max_pages]`` int32, max_pages =
+    ceil(max_seqlen_k / block_size), ready for :func:`paged_split_kv_attention`
+    on ``cache[:, 0]`` / ``cache[:, 1]``.  The cache buffer is reused by the next
+    call on the same stream.
+    """
+    if key_cache.ndim != 4 or value_cache.shape != key_cache.shape:
+        raise ValueError("expected key/value caches [num_blocks, block_size, kv_heads, >= head_dim]")
+    if key_cache.device.type != "cuda":
+        raise RuntimeError("dequantize_kv_pages runs on CUDA tensors only (no CPU path)")
+    elem = _DEQUANT_ELEM.get(key_cache.dtype)
+    if elem is None:
+        raise ValueError(f"no dequantisation for a {key_cache.dtype} cache")
+    if kv_quant_mode == _lib.KVQ_INT8_PER_TOKEN_HEAD and key_cache.dtype in (torch.int8, torch.uint8):
+        elem = _lib.DTYPE_I8
+    if kv_quant_mode == _lib.KVQ_FP8_PER_TENSOR:
+        if k_descale is None or v_descale is None:
+            raise ValueError("fp8 per-tensor caches need k_descale and v_descale")
+        k_scale = k_descale.to(device=key_cache.device, dtype=torch.float32).reshape(-1)[:1].contiguous()
+        v_scale = v_descale.to(device=key_cache.device, dtype=torch.float32).reshape(-1)[:1].contiguous()
+        ksc = vsc = None
+    else:
+        if k_scale_cache is None or v_scale_cache is None:
+            raise ValueError("per-token-head caches need k_scale_cache and v_scale_cache")
+        ksc, vsc = k_scale_cache, v_scale_cache
+        k_scale = v_scale = None
+    num_blocks, block_size, kv_heads, row = key_cache.shape
+    if head_dim > row or head_dim % 4 or key_cache.stride(3) != 1:
+        raise ValueError("cache rows must hold head_dim contiguous elements")
+    num_seqs = int(seqused_k.numel())
+    max_pages = max(1, -(-int(max_seqlen_k) // block_size))
+    dev = key_cache.device
+    n = num_seqs * max_pages * 2 * block_size * kv_heads * head_dim
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), _lib.current_stream(dev))
+    buf = _dense.get((key, out_dtype))
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(max(n, 1), dtype=out_dtype, device=dev)
+        _dense[(key, out_dtype)] = buf
+    cache = buf[:n].view(num_seqs * max_pages, 2, block_size, kv_heads, head_dim)
+    table = torch.empty(num_seqs, max_pages, dtype=torch.int32, device=dev)
+    if block_table.stride(1) != 1:
+        block_table = block_table.contiguous()
+    seqused_k = seqused_k.contiguous()
+    p = _lib.KvDequantParams(
+        key_cache=key_cache.data_ptr(), value_cache=value_cache.data_ptr(),
+        kc_stride_block=key_cache.stride(0), kc_stride_tok=key_cache.stride(1), kc_stride_head=key_cache.stride(2),
+        vc_stride_block=value_cache.stride(0), vc_stride_tok=value_cache.stride(1),
+        vc_stride_head=value_cache.stride(2),
+        k_scale=k_scale.data_ptr() if k_scale is not None else None,
+        v_scale=v_scale.data_ptr() if v_scale is not None else None,
+        k_scale_cache=ksc.data_ptr() if ksc is not None else None,
+        v_scale_cache=vsc.data_ptr() if vsc is not None else None,
+        ks_stride_block=ksc.stride(0) if ksc is not None else 0, ks_stride_tok=ksc.stride(1) if ksc is not None else 0,
+        ks_stride_head=ksc.stride(2) if ksc is not None else 0,
+        vs_stride_block=vsc.stride(0) if vsc is not None else 0, vs_stride_tok=vsc.stride(1) if vsc is not None else 0,
+        vs_stride_head=vsc.stride(2) if vsc is not None else 0,
+        block_table=block_table.data_ptr(), block_table_stride=block_table.stride(0),
+        block_table_cols=block_table.shape[1], block_table_dtype=_lib.dtype_code(block_table.dtype),
+        seqused_k=seqused_k.data_ptr(), seqlen_dtype=_lib.dtype_code(seqused_k.dtype),
+        out_cache=cache.data_ptr(), out_block_table=table.data_ptr(),
+        num_seqs=num_seqs, max_pages=max_pages, block_size=block_size, num_kv_heads=kv_heads, head_dim=head_dim,
+        num_blocks=num_blocks, cache_dtype=elem, quant_mode=int(kv_quant_mode), out_dtype=_lib.dtype_code(out_dtype),
+    )
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().b200_kv_dequant_pages(ctypes.byref(p), _lib.current_stream(dev)), "dequantize_kv_pages")
+    return cache, table
+

@@ -6,8 +6,9 @@ reference's integration patch adds it (``integration/vllm-plugin-FL-split-kv.pat
 * :func:`_run_unified_attention` (patch :88-141) -- the per-call route: the
   sm_100a Split-KV path when ``ILUVATAR_USE_OPTIMIZED`` and
   ``ILUVATAR_SPLIT_KV`` are both set ("1", "true" or "yes") and the call uses
-  no unsupported feature (KV quantisation, ALiBi, sinks, softcap, a sliding
-  window, any descale, tensor descriptors, non-causal), else vLLM's
+  no unsupported feature (ALiBi, sinks, softcap, a sliding window, a query
+  descale or a descale without an fp8 per-tensor cache, nvfp4, tensor
+  descriptors, non-causal), else vLLM's
   ``unified_attention``.  A head shape or dtype the sm_100a kernel does not
   run (``kernel_supports``: fp32, head_dim other than 64 / 128 / 256, more than
   128 query heads per KV head) takes the vLLM route too.  Pure decode (``max_seqlen_q <= 1``) stays on vLLM
@@ -24,6 +25,11 @@ reference's integration patch adds it (``integration/vllm-plugin-FL-split-kv.pat
   supported dtypes and block sizes).
 
 Differences from the reference, on purpose:
+
+* Quantised caches (fp8 per-tensor, int8 / fp8 per-token-head) take the
+  sm_100a path: the pages a call references are dequantised into a dense cache
+  in the query dtype (``b200_kv_dequant_pages``), then the same attention
+  kernel runs.  The reference sends every quantised cache to vLLM.
 
 * The k/v-descale guard.  For unquantised (auto / bf16 / fp16) caches the
   reference's ``forward`` passes ``layer._k_scale.expand(...)`` and
@@ -117,18 +123,24 @@ def _run_unified_attention(**kwargs: Any) -> torch.Tensor:
     """Use the sm_100a path for supported prefill / mixed (and, if enabled, decode) calls."""
     enabled = _flag("ILUVATAR_USE_OPTIMIZED") and _flag("ILUVATAR_SPLIT_KV")
     max_query_len = kwargs["max_seqlen_q"]
+    mode = KVQuantMode(int(kwargs.get("kv_quant_mode", KVQuantMode.NONE)))
+    # Descales belong to the fp8 per-tensor cache (its dequantisation scales);
+    # with any other cache they are a feature the sm_100a path does not have.
+    descaled = kwargs.get("k_descale") is not None or kwargs.get("v_descale") is not None
     unsupported = (
-        int(kwargs.get("kv_quant_mode", KVQuantMode.NONE)) != KVQuantMode.NONE
+        mode == KVQuantMode.NVFP4
+        or (mode == KVQuantMode.FP8_PER_TENSOR and not (kwargs.get("k_descale") is not None
+                                                       and kwargs.get("v_descale") is not None))
+        or (mode.is_per_token_head and (kwargs.get("k_scale_cache") is None or kwargs.get("v_scale_cache") is None))
+        or (descaled and mode != KVQuantMode.FP8_PER_TENSOR)
         or kwargs.get("alibi_slopes") is not None
         or kwargs.get("sinks") is not None
         or kwargs.get("softcap", 0.0) != 0.0
         or tuple(kwargs.get("window_size", (-1, -1))) != (-1, -1)
         or kwargs.get("q_descale") is not None
-        or kwargs.get("k_descale") is not None
-        or kwargs.get("v_descale") is not None
         or kwargs.get("use_td", False)
         or kwargs.get("causal") is not True
-        or not kernel_supports(kwargs["q"], kwargs["k"])
+        or not kernel_supports(kwargs["q"], kwargs["k"], int(mode))
     )
     decode_only = max_query_len <= 1
     if not enabled or unsupported or max_query_len < 1 or (decode_only and not _flag("ILUVATAR_SPLIT_KV_DECODE")):
@@ -151,6 +163,11 @@ def _run_unified_attention(**kwargs: Any) -> torch.Tensor:
         block_n_override=int(os.environ.get("ILUVATAR_BLOCK_N", "64")),
         launch_num_warps_override=int(os.environ.get("ILUVATAR_NUM_WARPS", "4")),
         launch_num_stages_override=int(os.environ.get("ILUVATAR_NUM_STAGES", "2")),
+        kv_quant_mode=int(mode),
+        k_descale=kwargs.get("k_descale"),
+        v_descale=kwargs.get("v_descale"),
+        k_scale_cache=kwargs.get("k_scale_cache"),
+        v_scale_cache=kwargs.get("v_scale_cache"),
     )
 
 

@@ -151,20 +151,34 @@ def split_kv_combine(o_splits: torch.Tensor, m_splits: torch.Tensor, l_splits: t
     return out
 
 
-def kernel_supports(q: torch.Tensor, k: torch.Tensor) -> bool:
-    """Whether the sm_100a kernel runs this call's head shape and element type.
+_QUANT_CACHE_DTYPES = {
+    1: (torch.float8_e4m3fn, torch.float8_e5m2, torch.uint8),  # fp8 per-tensor
+    2: (torch.int8, torch.uint8),                              # int8 per-token-head
+    3: (torch.float8_e4m3fn, torch.uint8),                     # fp8 per-token-head
+}
+
+
+def kernel_supports(q: torch.Tensor, k: torch.Tensor, kv_quant_mode: int = 0) -> bool:
+    """Whether the sm_100a kernels run this call's head shape and element types.
 
     ``q`` is ``[T, Hq, D]``; ``k`` is the 4-D ``[blocks, block, KH, D]`` cache
-    or the 5-D ``[blocks, 2, block, KH, D]`` one.  The dispatcher and the
-    service route calls for which this is false (fp32, head_dim other than
-    64 / 128 / 256, more than 128 query heads per KV head) to their baseline
-    kernel, as they route the features the kernel does not implement.
+    or the 5-D ``[blocks, 2, block, KH, D]`` one; a quantised cache
+    (``kv_quant_mode`` 1-3) holds 1-byte elements and is dequantised page by
+    page first.  The dispatcher and the service route calls for which this is
+    false (fp32, head_dim other than 64 / 128 / 256, more than 128 query heads
+    per KV head, an unknown quantisation) to their baseline kernel, as they
+    route the features the kernels do not implement.
     """
     try:
         code = _lib.dtype_code(q.dtype)
     except ValueError:
         return False
-    if q.ndim != 3 or k.ndim not in (4, 5) or k.dtype != q.dtype:
+    if q.ndim != 3 or k.ndim not in (4, 5):
+        return False
+    if kv_quant_mode:
+        if k.dtype not in _QUANT_CACHE_DTYPES.get(int(kv_quant_mode), ()):
+            return False
+    elif k.dtype != q.dtype:
         return False
     return bool(_lib.load().b200_attn_shape_supported(int(q.shape[1]), int(k.shape[-2]), int(q.shape[2]), code))
 

@@ -5,8 +5,12 @@ Mirrors ``unified_attention_optimized`` of the reference
 non-causal calls with ``ValueError``, resolves the split count from the
 override, then ``ILUVATAR_NUM_SPLITS``, then
 ``VLLM_ILUVATAR_ATTN_SPLIT_KV_SEGMENTS``, and swallows extra keyword
-arguments.  One difference: when none of the three is set the split count
-is chosen automatically (``0``) instead of the reference's fixed 4.
+arguments.  Differences: when none of the three is set the split count
+is chosen automatically (``0``) instead of the reference's fixed 4; and a
+quantised cache (``kv_quant_mode`` 1: fp8 per-tensor with ``k_descale`` /
+``v_descale``; 2 / 3: int8 / fp8 per-token-head with ``k_scale_cache`` /
+``v_scale_cache``), which the reference leaves to vLLM, is dequantised page by
+page (``b200_kv_dequant_pages``) and attended by the same kernel.
 """
 
 from __future__ import annotations
@@ -16,6 +20,7 @@ from typing import Optional
 
 import torch
 
+from .kv_cache import dequantize_kv_pages
 from .split_kv_paged import paged_split_kv_attention
 
 
@@ -45,10 +50,22 @@ def unified_attention_optimized(
     block_n_override: Optional[int] = None,
     launch_num_warps_override: Optional[int] = None,
     launch_num_stages_override: Optional[int] = None,
+    kv_quant_mode: int = 0,
+    k_descale: Optional[torch.Tensor] = None,
+    v_descale: Optional[torch.Tensor] = None,
+    k_scale_cache: Optional[torch.Tensor] = None,
+    v_scale_cache: Optional[torch.Tensor] = None,
     **kwargs,
 ) -> torch.Tensor:
     if causal is not True:
         raise ValueError("Split-KV currently supports causal attention only")
+    if kv_quant_mode:
+        # A quantised cache: the referenced pages dequantised into a dense
+        # cache in the query dtype, then the same kernel.
+        dense, block_table = dequantize_kv_pages(
+            k, v, block_table, seqused_k, max_seqlen_k, kv_quant_mode, q.dtype, q.shape[2],
+            k_descale=k_descale, v_descale=v_descale, k_scale_cache=k_scale_cache, v_scale_cache=v_scale_cache)
+        k, v = dense[:, 0], dense[:, 1]
     return paged_split_kv_attention(
         q=q,
         k=k,

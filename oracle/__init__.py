@@ -20,6 +20,7 @@ from .paged_sdpa import (
     split_kv_reduce_reference,
 )
 from .kv_cache import (
+    dequantize_cache_reference,
     fp8_decode,
     fp8_encode,
     kv_write_reference,
@@ -38,6 +39,7 @@ __all__ = [
     "rope_and_cache_reference",
     "rotate_fp32",
     "fp8_encode",
+    "dequantize_cache_reference",
     "fp8_decode",
     "quantize_per_tensor",
     "quantize_per_token_head",

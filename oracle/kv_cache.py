@@ -154,6 +154,31 @@ def kv_write_reference(
     return kc, vc, ksc, vsc
 
 
+def dequantize_cache_reference(cache_codes: torch.Tensor, kv_cache_dtype: str, head_dim: int,
+                               scale: float | None = None, scale_cache: torch.Tensor | None = None) -> torch.Tensor:
+    """The values vLLM's unified attention reads from a quantised cache, in fp32.
+
+    Follows vLLM 0.22 ``vllm/v1/attention/ops/triton_unified_attention.py``:
+    fp8 per-tensor (``_cast_kv_tile``, :39-55): ``fp8(x) * scale``; int8 / fp8
+    per-token-head (:469-511): the element times the scale of its (block,
+    slot, head), which vLLM folds into the logits (keys) and into P (values).
+    ``cache_codes [num_blocks, block_size, KH, >= head_dim]``: int8 values or
+    fp8 codes (uint8 / float8 storage).  Returns ``[num_blocks, block_size, KH,
+    head_dim]`` float32.
+    """
+    c = cache_codes.detach().cpu()[..., :head_dim]
+    if kv_cache_dtype.endswith("per_token_head"):
+        if kv_cache_dtype.startswith("int8"):
+            vals = c.view(torch.int8).float().numpy()
+        else:
+            vals = fp8_decode(c.contiguous().view(torch.uint8).numpy(), "e4m3")
+        s = scale_cache.detach().cpu().float().numpy()[..., None]
+        return torch.from_numpy((vals * s).astype(np.float32))
+    fmt = "e5m2" if kv_cache_dtype == "fp8_e5m2" else "e4m3"
+    vals = fp8_decode(c.contiguous().view(torch.uint8).numpy(), fmt)
+    return torch.from_numpy((vals * np.float32(scale)).astype(np.float32))
+
+
 def rope_and_cache_service_reference(
     query: torch.Tensor,
     key: torch.Tensor,

@@ -231,6 +231,25 @@ def test_dispatcher_routes_shapes_the_kernel_does_not_run_to_vllm(routes, monkey
     assert (len(optimized.calls), len(baseline.calls)) == ((1, 0) if optimized_route else (0, 1))
 
 
+def test_dispatcher_quantised_caches_take_the_dequantising_route(routes, monkeypatch):
+    """fp8 per-tensor with descales, int8 per-token-head with scale caches:
+    the optimized route, with the scales forwarded; without them: vLLM."""
+    baseline, optimized = routes
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    fp8 = torch.empty(4, 2, 16, 2, 128, dtype=torch.float8_e4m3fn, device="meta")
+    minicpm_b200.iluvatar_attention(**_dispatch_args(k=fp8, v=fp8, kv_quant_mode=1, k_descale=torch.ones(1, 2),
+                                                     v_descale=torch.ones(1, 2)))
+    assert len(optimized.calls) == 1 and optimized.calls[0]["kv_quant_mode"] == 1
+    assert optimized.calls[0]["k_descale"] is not None
+    i8 = torch.empty(4, 2, 16, 2, 132, dtype=torch.int8, device="meta")
+    sc = torch.ones(4, 16, 2)
+    minicpm_b200.iluvatar_attention(**_dispatch_args(k=i8, v=i8, kv_quant_mode=2, k_scale_cache=sc, v_scale_cache=sc))
+    assert len(optimized.calls) == 2 and optimized.calls[1]["k_scale_cache"] is sc
+    minicpm_b200.iluvatar_attention(**_dispatch_args(k=i8, v=i8, kv_quant_mode=2))
+    assert len(baseline.calls) == 1
+
+
 def test_dispatcher_optimized_route_and_5d_unbind(routes, monkeypatch):
     baseline, optimized = routes
     monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")

@@ -165,7 +165,9 @@ def test_forward_passes_no_descale_for_unquantised_caches(routes, monkeypatch):
     assert kw["k"].shape == (8, 16, 2, 128)  # kv_cache.unbind(1)
 
 
-def test_forward_fp8_cache_keeps_descales_and_stays_on_vllm(routes, monkeypatch):
+def test_forward_fp8_cache_passes_descales_to_the_dequantising_path(routes, monkeypatch):
+    """An fp8 per-tensor cache with its descales takes the sm_100a path (its
+    pages are dequantised first); the reference sent it to vLLM."""
     monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
     monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
     _, meta = _metadata()
@@ -173,9 +175,35 @@ def test_forward_fp8_cache_keeps_descales_and_stays_on_vllm(routes, monkeypatch)
     q = torch.zeros(8, 16, 128, dtype=torch.bfloat16)
     _impl("fp8").forward(_layer(), q, q, q, kv_cache, meta, torch.empty_like(q))
     name, kw = routes[-1]
-    assert name == "vllm"
+    assert name == "b200"
     assert kw["k_descale"].shape == (2, 2) and kw["k"].dtype == torch.float8_e4m3fn
     assert kw["kv_quant_mode"] == service.KVQuantMode.FP8_PER_TENSOR
+
+
+def test_forward_per_token_head_cache_takes_the_dequantising_path(routes, monkeypatch):
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    _, meta = _metadata()
+    kv_cache = torch.zeros(8, 2, 16, 2, 132, dtype=torch.int8)
+    q = torch.zeros(8, 16, 128, dtype=torch.bfloat16)
+    _impl("int8_per_token_head").forward(_layer(), q, q, q, kv_cache, meta, torch.empty_like(q))
+    name, kw = routes[-1]
+    assert name == "b200" and kw["kv_quant_mode"] == service.KVQuantMode.INT8_PER_TOKEN_HEAD
+    assert kw["k_scale_cache"].shape == (8, 16, 2) and kw["k_descale"] is None
+
+
+@pytest.mark.parametrize("over", [
+    dict(kv_quant_mode=service.KVQuantMode.NVFP4),
+    dict(kv_quant_mode=service.KVQuantMode.INT8_PER_TOKEN_HEAD),  # no scale caches
+    dict(kv_quant_mode=service.KVQuantMode.FP8_PER_TENSOR, k_descale=torch.ones(1)),  # no v_descale
+])
+def test_quantised_caches_without_what_they_need_stay_on_vllm(routes, monkeypatch, over):
+    monkeypatch.setenv("ILUVATAR_USE_OPTIMIZED", "1")
+    monkeypatch.setenv("ILUVATAR_SPLIT_KV", "1")
+    q, _ = _qk()
+    k = torch.empty(8, 16, 2, 128, dtype=torch.int8, device="meta")
+    service._run_unified_attention(**_kwargs(q=q, k=k, v=k, out=q, **over))
+    assert routes[-1][0] == "vllm"
 
 
 def test_forward_per_token_head_cache_sets_up_inline_scales(routes):

@@ -485,7 +485,8 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   sa.units = reinterpret_cast<int4*>(ws + w.units_off);
   sa.split_units = reinterpret_cast<int4*>(ws + w.split_units_off);
   sa.unit_count = reinterpret_cast<int*>(ws + w.count_off);
-  b200::attn_schedule_kernel<<<1, b200::kSchedThreads, 0, s>>>(sa);
+  cudaFuncSetAttribute(b200::attn_schedule_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, b200::kSchedSmemBytes);
+  b200::attn_schedule_kernel<<<1, b200::kSchedThreads, b200::kSchedSmemBytes, s>>>(sa);
   if (int r = check_launch("attn_schedule_kernel")) return r;
 
   b200::AttnKernelArgs a{};

@@ -930,7 +930,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 constexpr int kSchedThreads = 1024;
 constexpr int kSchedBuckets = 2048;
 constexpr float kSchedBucketsPerOctave = 46.0f;  // 2^44 (the largest work estimate) -> bucket 2024
-constexpr int kSchedSeqCache = 4096;  // sequences whose query-unit prefix is kept in shared memory
+constexpr int kSchedSeqCache = 4096;  // sequences whose arrays the schedule keeps in shared memory
 constexpr int kSplitBalance = 2;   // split units larger than half of one SM's share of the batch
 constexpr int kMinSplitTiles = 2;  // KV tiles each split keeps at least
 
@@ -1001,16 +1001,6 @@ __device__ __forceinline__ void buckets_to_offsets_desc(int* hist, int* warp_sum
   }
 }
 
-// Sort bucket of sequence b: log2 of (query units x mean causal key count),
-// the sequence's share of the work up to a constant.
-__device__ __forceinline__ int seq_bucket(const SchedArgs& a, int b, int units) {
-  const int ql = load_index(a.cu_q, b + 1, a.len_i64) - load_index(a.cu_q, b, a.len_i64);
-  const int L = load_index(a.seqused, b, a.len_i64);
-  const float keys = fmaxf(static_cast<float>(L) - 0.5f * static_cast<float>(ql), 1.0f);
-  const float work = static_cast<float>(units) * keys;
-  return min(kSchedBuckets - 1, max(0, static_cast<int>(__log2f(work) * kSchedBucketsPerOctave)));
-}
-
 // Last index i in [0, n) with v[i] <= x (v non-decreasing, v[0] <= x).
 __device__ __forceinline__ int upper_index(const int* v, int n, int x) {
   int lo = 0, hi = n - 1;
@@ -1037,13 +1027,35 @@ __device__ __forceinline__ int qunit_splits(const SchedArgs& a, int n, long long
   return (n + tps - 1) / tps;                                             // no split left empty
 }
 
+// Dynamic shared memory of the schedule kernel: the per-sequence arrays
+// (query-unit prefix, query length, KV length) for up to kSchedSeqCache
+// sequences and the per-query-unit arrays (splits, work-unit prefix, split
+// slot) for up to kSchedQunitCache query units; larger batches keep them in
+// the workspace.  Every pass then reads shared memory, and global memory is
+// read once per value.
+constexpr int kSchedQunitCache = 8192;
+constexpr uint32_t kSchedSmemBytes =
+    4 * (kSchedBuckets + 32 + 3 * kSchedSeqCache + 1 + 3 * kSchedQunitCache + 1);
+
 __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const SchedArgs a) {
-  __shared__ int hist[kSchedBuckets];
-  __shared__ int warp_sums[32];
-  __shared__ int s_tile_base[kSchedSeqCache + 1];
+  extern __shared__ int sched_smem[];
+  int* hist = sched_smem;                                // [kSchedBuckets]
+  int* warp_sums = hist + kSchedBuckets;                 // [32]
+  int* s_tb = warp_sums + 32;                            // [kSchedSeqCache + 1]
+  int* s_ql = s_tb + kSchedSeqCache + 1;                 // [kSchedSeqCache]
+  int* s_L = s_ql + kSchedSeqCache;                      // [kSchedSeqCache]
+  int* s_qs = s_L + kSchedSeqCache;                      // [kSchedQunitCache]
+  int* s_qb = s_qs + kSchedQunitCache;                   // [kSchedQunitCache + 1]
+  int* s_qslot = s_qb + kSchedQunitCache + 1;            // [kSchedQunitCache]
   __shared__ int s_total_qunits;
   __shared__ unsigned long long s_total_tiles;
   griddep_launch_dependents();  // the attention grid may launch; it waits for this one
+
+  const bool seq_cached = a.num_seqs <= kSchedSeqCache;
+  auto q_len = [&](int b) {
+    return seq_cached ? s_ql[b] : load_index(a.cu_q, b + 1, a.len_i64) - load_index(a.cu_q, b, a.len_i64);
+  };
+  auto kv_len = [&](int b) { return seq_cached ? s_L[b] : load_index(a.seqused, b, a.len_i64); };
 
   // 1. query units per sequence, exclusive prefix over sequences.
   int carry = 0;
@@ -1052,40 +1064,46 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
     int n = 0;
     if (b < a.num_seqs) {
       const int ql = load_index(a.cu_q, b + 1, a.len_i64) - load_index(a.cu_q, b, a.len_i64);
+      const int L = load_index(a.seqused, b, a.len_i64);
+      if (seq_cached) {
+        s_ql[b] = ql;
+        s_L[b] = L;
+      }
       n = ql > 0 ? (ql + a.pos_per_unit - 1) / a.pos_per_unit : 0;
     }
     int total;
     const int before = block_exclusive_scan(n, warp_sums, total);
     if (b < a.num_seqs) {
       a.tile_base[b] = carry + before;
-      if (b < kSchedSeqCache) s_tile_base[b] = carry + before;
+      if (seq_cached) s_tb[b] = carry + before;
     }
     carry += total;
   }
   if (threadIdx.x == 0) {
     a.tile_base[a.num_seqs] = carry;
-    if (a.num_seqs < kSchedSeqCache) s_tile_base[a.num_seqs] = carry;
+    if (seq_cached) s_tb[a.num_seqs] = carry;
     s_total_qunits = carry;
     s_total_tiles = 0ull;
   }
   for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;
   __syncthreads();
   const int nq = s_total_qunits;
-  // The query-unit prefix, searched once per query unit: from shared memory
-  // when the batch has at most kSchedSeqCache sequences.
-  const int* tb = a.num_seqs < kSchedSeqCache ? s_tile_base : a.tile_base;
+  const int* tb = seq_cached ? s_tb : a.tile_base;
+  const bool q_cached = nq <= kSchedQunitCache;
+  int* qs = q_cached ? s_qs : a.qunit_split;
+  int* qb = q_cached ? s_qb : a.qunit_base;
+  int* qslot = q_cached ? s_qslot : a.qunit_slot;
 
-  // 2. KV tiles of each query unit's whole key range (kept in qunit_split for
-  // now) and their sum over query units and KV heads.
+  // 2. KV tiles of each query unit's whole key range (kept in qs for now) and
+  // their sum over query units and KV heads.
   unsigned long long my_tiles = 0;
   for (int j = threadIdx.x; j < nq; j += kSchedThreads) {
     const int seq = upper_index(tb, a.num_seqs, j);
-    const int ql = load_index(a.cu_q, seq + 1, a.len_i64) - load_index(a.cu_q, seq, a.len_i64);
-    const int n = qunit_full_tiles(ql, load_index(a.seqused, seq, a.len_i64), j - tb[seq], a.pos_per_unit);
-    a.qunit_split[j] = n;
+    const int n = qunit_full_tiles(q_len(seq), kv_len(seq), j - tb[seq], a.pos_per_unit);
+    qs[j] = n;
     my_tiles += static_cast<unsigned long long>(n);
   }
-  atomicAdd(&s_total_tiles, my_tiles);
+  if (a.num_splits > 1) atomicAdd(&s_total_tiles, my_tiles);
   __syncthreads();
   const long long total_tiles = static_cast<long long>(s_total_tiles) * a.num_kv_heads;
 
@@ -1094,45 +1112,51 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   for (int base = 0; base < nq; base += kSchedThreads) {
     const int j = base + threadIdx.x;
     int s = 1;
-    if (j < nq) s = qunit_splits(a, a.qunit_split[j], total_tiles);
-    int utotal, stotal;
+    if (j < nq) s = qunit_splits(a, qs[j], total_tiles);
+    int utotal, stotal = 0;
     const int ubefore = block_exclusive_scan(j < nq ? s * a.num_kv_heads : 0, warp_sums, utotal);
-    const int sbefore = block_exclusive_scan(j < nq && s > 1 ? 1 : 0, warp_sums, stotal);
+    int sbefore = 0;
+    if (a.num_splits > 1) sbefore = block_exclusive_scan(j < nq && s > 1 ? 1 : 0, warp_sums, stotal);
     if (j < nq) {
-      a.qunit_split[j] = s;
-      a.qunit_base[j] = ucarry + ubefore;
-      a.qunit_slot[j] = s > 1 ? scarry + sbefore : -1;
+      qs[j] = s;
+      qb[j] = ucarry + ubefore;
+      qslot[j] = s > 1 ? scarry + sbefore : -1;
     }
     ucarry += utotal;
     scarry += stotal;
   }
-  if (threadIdx.x == 0) a.qunit_base[nq] = ucarry;
+  if (threadIdx.x == 0) qb[nq] = ucarry;
   __syncthreads();
   const int total_units = min(ucarry, a.capacity);
 
   // 4. units per work bucket; each sequence takes a contiguous range of its bucket.
-  auto seq_units = [&](int b) { return a.qunit_base[tb[b + 1]] - a.qunit_base[tb[b]]; };
+  auto seq_bucket_of = [&](int b, int units) {
+    const float keys = fmaxf(static_cast<float>(kv_len(b)) - 0.5f * static_cast<float>(q_len(b)), 1.0f);
+    const float work = static_cast<float>(units) * keys;
+    return min(kSchedBuckets - 1, max(0, static_cast<int>(__log2f(work) * kSchedBucketsPerOctave)));
+  };
+  auto seq_units = [&](int b) { return qb[tb[b + 1]] - qb[tb[b]]; };
   for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
     const int qt = tb[b + 1] - tb[b];
-    if (qt > 0) atomicAdd(&hist[seq_bucket(a, b, qt)], seq_units(b));
+    if (qt > 0) atomicAdd(&hist[seq_bucket_of(b, qt)], seq_units(b));
   }
   __syncthreads();
   buckets_to_offsets_desc(hist, warp_sums);
   __syncthreads();
   for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
     const int qt = tb[b + 1] - tb[b];
-    if (qt > 0) a.seq_off[b] = atomicAdd(&hist[seq_bucket(a, b, qt)], seq_units(b));
+    if (qt > 0) a.seq_off[b] = atomicAdd(&hist[seq_bucket_of(b, qt)], seq_units(b));
   }
   __syncthreads();
   // 5. scatter, one query unit per thread: its units (KV head, then split)
   // go to its sequence's range, the sequence's last query unit first.
   for (int j = threadIdx.x; j < nq; j += kSchedThreads) {
     const int seq = upper_index(tb, a.num_seqs, j);
-    const int s = a.qunit_split[j];
-    const int first = a.qunit_base[j];
+    const int s = qs[j];
+    const int first = qb[j];
     const int qunit = j - tb[seq];
-    const int pos0 = a.seq_off[seq] + (a.qunit_base[tb[seq + 1]] - a.qunit_base[j + 1]);
-    const int slot0 = s > 1 ? a.qunit_slot[j] * a.num_kv_heads : -1;
+    const int pos0 = a.seq_off[seq] + (qb[tb[seq + 1]] - qb[j + 1]);
+    const int slot0 = s > 1 ? qslot[j] * a.num_kv_heads : -1;
     for (int rem = 0; rem < s * a.num_kv_heads && first + rem < total_units; ++rem) {
       const int kvh = rem / s;
       const int split = rem - kvh * s;
@@ -1154,8 +1178,8 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
     unit = a.units[tail0 + threadIdx.x];
     int kvh, split, nsplit;
     unpack_unit(unit, kvh, split, nsplit);
-    const UnitGeom g = unit_geometry(load_index(a.cu_q, unit.x, a.len_i64), load_index(a.cu_q, unit.x + 1, a.len_i64),
-                                     load_index(a.seqused, unit.x, a.len_i64), unit.y, split, nsplit, a.pos_per_unit);
+    const int q0 = seq_cached ? 0 : load_index(a.cu_q, unit.x, a.len_i64);
+    const UnitGeom g = unit_geometry(q0, q0 + q_len(unit.x), kv_len(unit.x), unit.y, split, nsplit, a.pos_per_unit);
     bucket = min(g.n_tiles, kSchedBuckets - 1);
   }
   for (int i = threadIdx.x; i < kSchedBuckets; i += kSchedThreads) hist[i] = 0;

@@ -579,11 +579,22 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
     c.pos_per_unit = sa.pos_per_unit;
     const int rows_per_block = b200::kCombineThreads / (p->head_dim / 8);
     const int64_t blocks_ub = (w.slots_ub * b200::kUnitRows + rows_per_block - 1) / rows_per_block;
-    const dim3 cgrid((unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks_ub, (int64_t)sm_count() * 8)));
-#define B200_UCOMB_S(T, D)                                                                                       \
-  if (splits <= 4) b200::unit_combine_kernel<T, D, 4><<<cgrid, b200::kCombineThreads, 0, s>>>(c);               \
-  else if (splits <= 8) b200::unit_combine_kernel<T, D, 8><<<cgrid, b200::kCombineThreads, 0, s>>>(c);          \
-  else b200::unit_combine_kernel<T, D, 16><<<cgrid, b200::kCombineThreads, 0, s>>>(c);
+    // One CTA per SM at most (grid-stride over the split rows); launched as a
+    // programmatic dependent of the attention kernel, so a call whose units
+    // were not split pays little more than the launch.
+    cudaLaunchAttribute cpdl[1];
+    cpdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    cpdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t ccfg{};
+    ccfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks_ub, (int64_t)sm_count())));
+    ccfg.blockDim = dim3(b200::kCombineThreads);
+    ccfg.stream = s;
+    ccfg.attrs = cpdl;
+    ccfg.numAttrs = 1;
+#define B200_UCOMB_S(T, D)                                                                     \
+  if (splits <= 4) cudaLaunchKernelEx(&ccfg, b200::unit_combine_kernel<T, D, 4>, c);          \
+  else if (splits <= 8) cudaLaunchKernelEx(&ccfg, b200::unit_combine_kernel<T, D, 8>, c);     \
+  else cudaLaunchKernelEx(&ccfg, b200::unit_combine_kernel<T, D, 16>, c);
 #define B200_UCOMB_D(T)                                                                          \
   if (p->head_dim == 64) { B200_UCOMB_S(T, 64) } else if (p->head_dim == 128) { B200_UCOMB_S(T, 128) } \
   else { B200_UCOMB_S(T, 256) }

@@ -896,6 +896,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  griddep_launch_dependents();  // the split-unit combine may launch (it waits for this grid to finish)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kAttnTmemCols);
@@ -1225,6 +1226,7 @@ template <typename T, int D, int kS>
 __global__ void __launch_bounds__(kCombineThreads) unit_combine_kernel(const UnitCombineArgs a) {
   constexpr int kThreadsPerRow = D / 8;
   constexpr int kRowsPerBlock = kCombineThreads / kThreadsPerRow;
+  griddep_wait();  // launched as a programmatic dependent of the attention kernel
   const int64_t rows = static_cast<int64_t>(a.unit_count[2]) * kUnitRows;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock; base < rows;
        base += static_cast<int64_t>(gridDim.x) * kRowsPerBlock) {

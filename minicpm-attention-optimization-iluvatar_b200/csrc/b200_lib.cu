@@ -579,14 +579,15 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
     c.pos_per_unit = sa.pos_per_unit;
     const int rows_per_block = b200::kCombineThreads / (p->head_dim / 8);
     const int64_t blocks_ub = (w.slots_ub * b200::kUnitRows + rows_per_block - 1) / rows_per_block;
-    // One CTA per SM at most (grid-stride over the split rows); launched as a
+    // Eight CTAs per SM at most (grid-stride over the split rows: enough rows
+    // in flight to stream the partials at HBM speed); launched as a
     // programmatic dependent of the attention kernel, so a call whose units
     // were not split pays little more than the launch.
     cudaLaunchAttribute cpdl[1];
     cpdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     cpdl[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t ccfg{};
-    ccfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks_ub, (int64_t)sm_count())));
+    ccfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks_ub, (int64_t)sm_count() * 8)));
     ccfg.blockDim = dim3(b200::kCombineThreads);
     ccfg.stream = s;
     ccfg.attrs = cpdl;

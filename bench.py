@@ -77,7 +77,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub", action="store_true",
                     help="16K workload: skip the 4K / mixed / RoPE / combine entries of the line's \"sub\" object")
-    ap.add_argument("--verify", action="store_true", help="gather outputs to rank 0 (NCCL) and check sampled rows")
+    ap.add_argument("--verify", action="store_true",
+                    help="gather outputs to rank 0 (NCCL) and compare with one single-GPU call (default with >1 GPU)")
+    ap.add_argument("--no-verify", action="store_true", help="skip that comparison with more than one GPU")
     return ap.parse_args()
 
 
@@ -627,11 +629,11 @@ def combine_bench(args, world, rank, local):
 
 
 # --------------------------------------------------------------------- verification
-def verify_sharded(args, batch, out, world, rank, splits):
+def verify_sharded(workload, num_seqs, batch, out, world, rank, splits):
     """Gather every rank's rows on rank 0 (NCCL) and compare them with one
     single-GPU call over the whole batch: a sequence's output does not depend
     on which rank or which physical pages hold it, so they must match bit for
-    bit."""
+    bit.  Returns the result on rank 0 (None elsewhere); raises on a mismatch."""
     import torch.distributed as dist
 
     from minicpm_b200 import paged_split_kv_attention, workloads
@@ -644,11 +646,11 @@ def verify_sharded(args, batch, out, world, rank, splits):
     else:
         ids = [list(batch.seq_ids)]
     if rank != 0:
-        return
+        return None
     order = [i for part in ids for i in part]
-    q, kv = workloads.WORKLOADS[args.workload]()
-    if args.num_seqs:
-        q, kv = q[: args.num_seqs], kv[: args.num_seqs]
+    q, kv = workloads.WORKLOADS[workload]()
+    if num_seqs:
+        q, kv = q[:num_seqs], kv[:num_seqs]
     ref = workloads.build_attention_batch([q[i] for i in order], [kv[i] for i in order], seq_ids=order,
                                           head_dim=HEAD_DIM).to(full.device)
     want = torch.empty_like(ref.q)
@@ -656,9 +658,9 @@ def verify_sharded(args, batch, out, world, rank, splits):
                              ref.cu_seqlens_q, ref.max_seqlen_q, ref.max_seqlen_k, ref.softmax_scale, num_splits=splits)
     torch.cuda.synchronize()
     same = bool(torch.equal(full, want))
-    print(json.dumps({"verify_rows": int(full.shape[0]), "verify_bit_identical": same}), flush=True)
     if not same:
         raise SystemExit("sharded output differs from the single-GPU output")
+    return {"rows": int(full.shape[0]), "bit_identical_to_one_gpu": same, "gather": "NCCL all_gather to rank 0"}
 
 
 # --------------------------------------------------------------------- e2e (host buffers)
@@ -923,6 +925,9 @@ def sub_benchmarks(args, world, rank, local) -> dict:
                 os.environ["B200_ATTN_SPLIT_UNIFORM"] = "1"
             try:
                 r = attention_run(workload, splits, steps, warmup, world, rank, local, clocks=False)
+                verify = None
+                if workload == "mixed_256" and world > 1 and not args.no_verify:
+                    verify = verify_sharded(workload, 0, r["batch"], r["out"], world, rank, splits)
             finally:
                 os.environ.pop("B200_ATTN_SPLIT_UNIFORM", None)
             achieved = r["local_flops"] / (r["launch_ms"] * 1e-3) / 1e12
@@ -936,6 +941,8 @@ def sub_benchmarks(args, world, rank, local) -> dict:
                              "traffic": traffic_per_launch(workload) if splits == 0 else None,
                              "peak_kind": f"bf16_tflops (burst) of {kind}", "per_launch_ms": r["launch_ms"]},
             }
+            if verify:
+                subs[name]["verify"] = verify
             del r
             torch.cuda.empty_cache()
         for rd in (64, 128):
@@ -979,8 +986,9 @@ def attention_bench(args, world, rank, local):
     if not args.no_e2e:
         e2e = e2e_pipelined(args, batch, out, args.splits, stream, world, total_flops, total_tokens)
 
-    if args.verify:
-        verify_sharded(args, batch, out, world, rank, args.splits)
+    verify = None
+    if args.verify or (world > 1 and not args.no_verify):
+        verify = verify_sharded(args.workload, args.num_seqs, batch, out, world, rank, args.splits)
 
     subs = None
     if args.workload == "chunked_prefill_16k" and not args.no_sub and not args.num_seqs and HEAD_DIM == 128:
@@ -1036,6 +1044,8 @@ def attention_bench(args, world, rank, local):
     }
     if world > 1:
         line["rank0_ms_per_step"] = sum(r["per_launch"]) / args.steps
+    if verify:
+        line["verify"] = verify
     if decode:
         # Decode streams every K/V row once for a handful of query rows: the
         # bound is HBM, and the metric is the bytes moved per second.

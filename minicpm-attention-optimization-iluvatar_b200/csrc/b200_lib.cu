@@ -202,7 +202,7 @@ int encode_kv_head_maps(const B200AttnParams* p, CUtensorMapDataType dt, b200::K
       const cuuint64_t dims[5] = {64, 8, (cuuint64_t)(p->head_dim / 64), (cuuint64_t)(p->block_size / 8),
                                   (cuuint64_t)p->num_blocks};
       const cuuint64_t strides[4] = {(cuuint64_t)(st * elt), 128, (cuuint64_t)(8 * st * elt), (cuuint64_t)(sb * elt)};
-      const cuuint32_t box[5] = {64, 8, 2, 2, 1};
+      const cuuint32_t box[5] = {64, 8, (cuuint32_t)std::min(2, p->head_dim / 64), 2, 1};
       if (int r = encode_map(kv ? &maps->v[h] : &maps->k[h], dt, 5, base, dims, strides, box, kv ? "v" : "k")) return r;
     }
   }
@@ -394,12 +394,11 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   if (p->block_size <= 0 || p->block_size % 16) return fail(B200_ERR_INVALID, "unsupported head shape for paged Split-KV");
   if (p->head_dim != 64 && p->head_dim != 128 && p->head_dim != 256)
     return fail(B200_ERR_INVALID, "unsupported head shape for paged Split-KV");
-  // head_dim 64 runs the head_dim-128 kernel: the tensor maps describe the
-  // real 64-element rows, so the second 64-column half of every Q, K and V
-  // box lies outside them and TMA fills it with zeros; S and P V are then
-  // exactly those of head_dim 64, and the epilogue stores 64 columns.
-  // head_dim 256 runs the kernel's wide variant (one query tile per unit).
+  // head_dim 64 runs the kernel's narrow variant (K/V half-slots, K = 64 S
+  // UMMAs, N = 64 P V UMMAs), head_dim 256 its wide variant (one query tile
+  // per unit).
   const bool wide = p->head_dim == 256;
+  const bool narrow = p->head_dim == 64;
   const int group = p->num_q_heads / p->num_kv_heads;
   if (group > b200::kAttnTileM)
     return fail(B200_ERR_UNSUPPORTED, "query heads per KV head (%d) must be at most 128", group);
@@ -456,8 +455,8 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   }
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Per-KV-head maps (4 KB boxes) when they fit; they assume full 128-column rows.
-  const bool head_maps = p->num_kv_heads <= b200::kMaxHeadMaps && p->head_dim != 64;
+  // Per-KV-head maps (16-key page-slice boxes) when they fit.
+  const bool head_maps = p->num_kv_heads <= b200::kMaxHeadMaps;
   b200::KvHeadMaps maps;
   if (head_maps) {
     if (int r = encode_kv_head_maps(p, dt, &maps)) return r;
@@ -547,14 +546,19 @@ int b200_paged_attn_fwd(const B200AttnParams* p, void* stream) {
   };
   const bool bf16 = p->dtype == B200_DTYPE_BF16;
   int lr;
-#define B200_ATTN_LAUNCH(HM, WIDE)                                                                 \
-  lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, HM, WIDE>, tm_q, maps, a)          \
-            : launch(b200::paged_attn_fwd_kernel<__half, HM, WIDE>, tm_q, maps, a);
+#define B200_ATTN_LAUNCH(HM, WIDE, NARROW)                                                           \
+  lr = bf16 ? launch(b200::paged_attn_fwd_kernel<__nv_bfloat16, HM, WIDE, NARROW>, tm_q, maps, a)    \
+            : launch(b200::paged_attn_fwd_kernel<__half, HM, WIDE, NARROW>, tm_q, maps, a);
+#define B200_ATTN_MAPS(WIDE, NARROW) \
+  if (head_maps) { B200_ATTN_LAUNCH(true, WIDE, NARROW) } else { B200_ATTN_LAUNCH(false, WIDE, NARROW) }
   if (wide) {
-    if (head_maps) { B200_ATTN_LAUNCH(true, true) } else { B200_ATTN_LAUNCH(false, true) }
+    B200_ATTN_MAPS(true, false)
+  } else if (narrow) {
+    B200_ATTN_MAPS(false, true)
   } else {
-    if (head_maps) { B200_ATTN_LAUNCH(true, false) } else { B200_ATTN_LAUNCH(false, false) }
+    B200_ATTN_MAPS(false, false)
   }
+#undef B200_ATTN_MAPS
 #undef B200_ATTN_LAUNCH
   if (lr != B200_OK) return lr;
   if (int r = check_launch("paged_attn_fwd_kernel")) return r;

@@ -169,8 +169,9 @@ struct KvHeadMaps {
 // Shared-memory offset of the 16-byte piece `chunk` of row r (a key) of half h
 // in one K/V ring slot.  Per-head maps: 8-key groups of 2 KB, each holding both
 // halves (8 rows of 128 B each); 4-D maps: two 16 KB halves of 128 rows.
-template <bool kHeadMaps>
+template <bool kHeadMaps, bool kNarrow = false>
 __device__ __forceinline__ uint32_t kv_slot_offset(int r, int h, int chunk) {
+  if (kNarrow) return r * 128 + chunk * 16;  // head_dim 64: one 64-column half, 128 B rows (both map kinds)
   return kHeadMaps ? (r >> 3) * 2048 + h * 1024 + (r & 7) * 128 + chunk * 16 : h * 16384 + r * 128 + chunk * 16;
 }
 
@@ -253,7 +254,11 @@ __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
 // kernel's slot layout -- so S = Q K^T is 16 UMMAs over two K slots and
 // O += P V two N = 128 UMMA chains, one per V half.  The second softmax
 // warpgroup has no tile and idles.
-template <typename T, bool kHeadMaps, bool kWide>
+//
+// kNarrow: head_dim 64.  K/V tiles fill the first 16 KB of their ring slots (one
+// 64-column half per row), S = Q K^T is 4 UMMAs (K = 64) and O += P V runs with
+// N = 64 (O in the first 64 of the tile's 128 TMEM columns).
+template <typename T, bool kHeadMaps, bool kWide, bool kNarrow>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     paged_attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ KvHeadMaps maps,
                           const AttnKernelArgs a) {
@@ -400,6 +405,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
               for (int q4 = 0; q4 < 4; ++q4)
                 tma_load_3d(sbase + kSmQ + q4 * 16384, &tm_q, bar(BAR_Q_FULL), 64 * q4, head0, t0);
+            } else if (kNarrow) {  // one 64-column box per tile
+              mbar_arrive_expect_tx(bar(BAR_Q_FULL), (two ? 2 : 1) * q_rows * 128);
+              tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q_FULL), 0, head0, t0);
+              if (two) tma_load_3d(sbase + kSmQ + 32768, &tm_q, bar(BAR_Q_FULL), 0, head0, t0 + P);
             } else {
               mbar_arrive_expect_tx(bar(BAR_Q_FULL), (two ? 2 : 1) * q_rows * 256);  // 2 halves of 128 B rows
               tma_load_3d(sbase + kSmQ, &tm_q, bar(BAR_Q_FULL), 0, head0, t0);
@@ -438,13 +447,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             of_cur = of_nxt;
             if (j + 1 < n_tiles) lookup(j + 1, pg_nxt, of_nxt);
           }
-          // 4-D maps: lanes 0..15 issue half c = lane & 1 of slice (lane >> 1).
-          const int c = (lane >> 1) & 7;
+          // 4-D maps: lanes 0..15 issue half lane & 1 of slice (lane >> 1); head_dim 64: lane c < 8 slice c.
+          const int c = kNarrow ? (lane & 7) : ((lane >> 1) & 7);
           const int page = kHeadMaps ? pg_cur : __shfl_sync(0xffffffffu, pg_cur, c);
           const int off = kHeadMaps ? of_cur : __shfl_sync(0xffffffffu, of_cur, c);
           if (lane == 0) {
             ok = mbar_wait(bar(BAR_KV_EMPTY + slot), ph ^ 1, abort_flag);
-            if (ok) mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), 32768);
+            if (ok) mbar_arrive_expect_tx(bar(BAR_KV_FULL + slot), kNarrow ? 16384 : 32768);
           }
           if (!__shfl_sync(0xffffffffu, ok, 0)) {  // also orders the expect_tx before the copies
             stop = true;
@@ -454,11 +463,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // lane c < 8 issues slice c (its own lookup): 16 keys x both halves.
             if (lane < 8) {
               const CUtensorMap* map = is_v ? &maps.v[e.kvh] : &maps.k[e.kvh];
-              tma_load_5d(sbase + kSmKV + slot * 32768 + lane * 4096, map, bar(BAR_KV_FULL + slot), 0, 0, 2 * hi,
-                          off >> 3, page);
+              tma_load_5d(sbase + kSmKV + slot * 32768 + lane * (kNarrow ? 2048 : 4096), map,
+                          bar(BAR_KV_FULL + slot), 0, 0, 2 * hi, off >> 3, page);
             }
-          } else if (lane < 16) {
-            const int half = lane & 1;
+          } else if (lane < (kNarrow ? 8 : 16)) {
+            const int half = kNarrow ? 0 : (lane & 1);
             const CUtensorMap* map = is_v ? &maps.v[0] : &maps.k[0];
             tma_load_4d(sbase + kSmKV + slot * 32768 + half * 16384 + c * 2048, map, bar(BAR_KV_FULL + slot),
                         half * 64 + hi * 128, off, e.kvh, page);
@@ -481,7 +490,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (warp == 1 && lane == 0) {
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_qk = umma_idesc_f16(kBF16, 128, 128, false, false);
-      constexpr uint32_t idesc_pv = umma_idesc_f16(kBF16, 128, 128, false, true);
+      constexpr uint32_t idesc_pv = umma_idesc_f16(kBF16, 128, kNarrow ? 64 : 128, false, true);
+      constexpr int kQkSteps = kNarrow ? 4 : 8;  // K = 16 per UMMA over head_dim (64 or 128)
+      constexpr uint32_t kKvSbo = kNarrow ? 1024 : (kHeadMaps ? 2048 : 1024);  // bytes between 8-key groups
       int fills = 0, q_uses = 0;
       int tiles_done[2] = {0, 0};  // tiles already processed by query-tile group t
       // Descriptors are built once per operand tile; the UMMAs of a tile step
@@ -491,17 +502,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // core, which takes only about one UMMA ahead of execution.
       auto issue_s = [&](int t, uint32_t kslot_addr) {
         const uint64_t qd = umma_desc_sw128(sbase + kSmQ + t * 32768, 16, 1024);
-        const uint64_t kd = umma_desc_sw128(kslot_addr, 16, kHeadMaps ? 2048 : 1024);
+        const uint64_t kd = umma_desc_sw128(kslot_addr, 16, kKvSbo);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < kQkSteps; ++kk) {
           const uint32_t qoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          const uint32_t koff = kv_slot_offset<kHeadMaps>(0, kk >> 2, 0) + (kk & 3) * 32;
+          const uint32_t koff = kv_slot_offset<kHeadMaps, kNarrow>(0, kk >> 2, 0) + (kk & 3) * 32;
           umma_ss(tmem + t * 128, qd + (qoff >> 4), kd + (koff >> 4), idesc_qk, kk > 0);
         }
         tc_commit(bar(BAR_S_FULL + t));
       };
       auto issue_pv = [&](int t, int c, uint32_t vslot_addr, bool acc, bool last) {
-        const uint64_t vd = umma_desc_sw128(vslot_addr, kHeadMaps ? 1024 : 16384, kHeadMaps ? 2048 : 1024);
+        const uint64_t vd = umma_desc_sw128(vslot_addr, kNarrow ? 16 : (kHeadMaps ? 1024 : 16384), kKvSbo);
         for (int q = 0; q < 4; ++q) {
           if (q % 2 == 0) {  // P is published in halves of 64 keys
             if (!mbar_wait(bar(BAR_P_FULL + 2 * t + q / 2), c & 1, abort_flag)) return false;
@@ -512,7 +523,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const int kk = 2 * q + h;
             // V is the MN-major B operand: 64-column atoms at LBO, 8-key groups at SBO.
             umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                    vd + (kv_slot_offset<kHeadMaps>(16 * kk, 0, 0) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
+                    vd + (kv_slot_offset<kHeadMaps, kNarrow>(16 * kk, 0, 0) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
           }
         }
         if (last) tc_commit(bar(BAR_O_DONE + t));  // the epilogue's wait; earlier tiles need none
@@ -773,7 +784,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             // S_FULL phase of tile j already implies PV_{j-1} is complete: its
             // commit covers every UMMA the issuer started before S_j.
 #pragma unroll 1
-            for (int c8 = 0; c8 < (kWide ? 16 : 8); ++c8) {  // O, 16 columns at a time
+            for (int c8 = 0; c8 < (kWide ? 16 : kNarrow ? 4 : 8); ++c8) {  // O, 16 columns at a time
               uint32_t o[16];
               tmem_ld16(o_addr + 16 * c8, o);
               tmem_wait_ld16(o);
@@ -801,11 +812,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               break;
             }
             const uint32_t vbase = sbase + kSmKV + (vidx % kKvStages) * 32768;
-            const int n16 = (v_tail_to - v_tail_from) * 16;  // 16-byte pieces over both halves
+            constexpr int kHalves = kNarrow ? 1 : 2;  // 64-column halves per row in a slot
+            const int n16 = (v_tail_to - v_tail_from) * 8 * kHalves;  // 16-byte pieces
             for (int i = threadIdx.x - 128; i < n16; i += 128) {
-              const int r = v_tail_from + (i >> 4);
-              const int half = (i >> 3) & 1;
-              st_shared_v4(vbase + kv_slot_offset<kHeadMaps>(r, half, i & 7), 0u, 0u, 0u, 0u);
+              const int r = v_tail_from + i / (8 * kHalves);
+              const int half = (i >> 3) & (kHalves - 1);
+              st_shared_v4(vbase + kv_slot_offset<kHeadMaps, kNarrow>(r, half, i & 7), 0u, 0u, 0u, 0u);
             }
           }
           if (!landed) {
@@ -867,7 +879,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
 #pragma unroll
-      for (int c4 = 0; c4 < (kWide ? 8 : 4); ++c4) {
+      for (int c4 = 0; c4 < (kWide ? 8 : kNarrow ? 2 : 4); ++c4) {
         if (c4 * 32 >= a.head_dim) break;  // warp-uniform: only the row's real columns
         uint32_t o[32];
         if (n_tiles > 0) {

@@ -311,15 +311,36 @@ def test_split_combine_shapes_against_oracle(head_dim, num_splits, partial_dtype
     assert (got - want).abs().max().item() <= tol
 
 
-@pytest.mark.parametrize("hq,hkv", [(16, 2), (8, 8), (16, 1)])
+@pytest.mark.parametrize("hq,hkv", [(16, 2), (8, 8), (16, 1), (12, 2), (32, 16)])
 def test_head_dim_64_against_oracle(hq, hkv):
-    """head_dim 64 (accepted by the reference wrapper): the head_dim-128 kernel
-    with the upper half of every Q/K/V box zero-filled by TMA, 64 columns
-    stored; partial pages, a decode row, splits 1 / 4 / auto."""
-    batch = small_batch([37, 1, 100, 16], [200, 63, 1000, 0], seed=64, num_q_heads=hq, num_kv_heads=hkv, head_dim=64)
+    """head_dim 64 (accepted by the reference wrapper): the kernel's narrow
+    variant (K/V half-slots, K = 64 S UMMAs, N = 64 P V UMMAs), with per-KV-head
+    maps and, at 16 KV heads, the 4-D maps; partial pages, a decode row,
+    splits 1 / 4 / auto and every unit split 4 ways."""
+    batch = small_batch([37, 1, 100, 16, 300], [200, 63, 1000, 0, 2500], seed=64, num_q_heads=hq, num_kv_heads=hkv,
+                        head_dim=64)
     want = oracle(batch)
     for s in (1, 4, 0):
         assert_close(run_gpu(batch, s), want, f"d64 {hq}/{hkv} S={s}")
+    with pytest.MonkeyPatch.context() as mp:
+        mp.setenv("B200_ATTN_SPLIT_UNIFORM", "1")
+        assert_close(run_gpu(batch, 4), want, f"d64 {hq}/{hkv} uniform S=4")
+    _no_device_error()
+
+
+def test_head_dim_64_chunked_prefill():
+    """head_dim 64 on 8 sequences of the 4K config: sampled rows of every
+    sequence against the oracle, and NaN in the page tails."""
+    q, kv = lengths_chunked_4k(num_seqs=8)
+    batch = build_attention_batch(q, kv, head_dim=64)
+    want, rows = sampled_oracle(batch, sample_blocks(q))
+    assert_close(run_gpu(batch, 0)[rows], want, "d64 4k")
+    cache = batch.kv_cache.clone()
+    for row, L in enumerate(batch.kv_lens):
+        if L % 16:
+            cache[int(batch.block_table[row, (L - 1) // 16]), :, L % 16:] = float("nan")
+    batch.kv_cache = cache
+    assert_close(run_gpu(batch, 0)[rows], want, "d64 4k nan tails")
     _no_device_error()
 
 

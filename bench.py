@@ -1016,7 +1016,6 @@ def attention_bench(args, world, rank, local):
             cpu = {"value": flops_s / statistics.mean(ts) / 1e12, "unit": "TFLOP/s",
                    "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
     config = attention_config(args.workload, world, args.splits, args.num_seqs)
-    config["timing"] = "one CUDA graph of the K calls" if args.graph else "K calls launched from Python"
     line = {
         "metric": METRIC,
         "value": r["value"],
@@ -1033,6 +1032,7 @@ def attention_bench(args, world, rank, local):
         "tokens_per_s": r["tokens_per_s"],
         "tc_peak_frac": r["value"] / world / peaks["bf16_tflops"],
         "config": config,
+        "timing": "one CUDA graph of the K calls" if args.graph else "K calls launched from Python",
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"], "traffic": traffic_per_launch(args.workload),
                      "peak_kind": f"bf16_tflops (burst) of {peak_kind}",

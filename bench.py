@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--splits", type=int, default=0, help="0 = automatic")
     ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128, 256],
                     help="attention workloads: head size (the headline is 128)")
+    ap.add_argument("--kv-quant", default="none", choices=["none", "fp8"],
+                    help="attention workloads: an fp8 per-tensor KV cache (pages dequantised, then the kernel)")
     ap.add_argument("--num-seqs", type=int, default=0,
                     help="keep only the first N sequences of the workload (small cases for profiling)")
     ap.add_argument("--rotary-dim", type=int, default=128)
@@ -804,7 +806,7 @@ def e2e_pipelined(args, batch, out, splits, stream, world, total_flops, total_to
 
 # --------------------------------------------------------------------- attention bench
 def attention_run(workload: str, splits: int, steps: int, warmup: int, world: int, rank: int, local: int,
-                  num_seqs: int = 0, graph: bool = False, clocks: bool = True) -> dict:
+                  num_seqs: int = 0, graph: bool = False, clocks: bool = True, kv_quant: str = "none") -> dict:
     """Device-resident timing of ``steps`` back-to-back calls on this rank's shard.
 
     Barrier + synchronize on both sides of the timed region, CUDA events on the
@@ -829,6 +831,21 @@ def attention_run(workload: str, splits: int, steps: int, warmup: int, world: in
     def step():
         paged_split_kv_attention(g.q, g.kv_cache[:, 0], g.kv_cache[:, 1], out, g.block_table, g.seqused_k,
                                  g.cu_seqlens_q, g.max_seqlen_q, g.max_seqlen_k, g.softmax_scale, num_splits=splits)
+
+    if kv_quant == "fp8":
+        # The same pages as an fp8 e4m3 cache with per-tensor scales: each call
+        # dequantises the pages it references, then runs the same kernel.
+        from minicpm_b200 import unified_attention_optimized
+
+        ks = torch.tensor([0.02], device=dev)
+        vs = torch.tensor([0.02], device=dev)
+        kc8 = (g.kv_cache[:, 0].float() / ks).to(torch.float8_e4m3fn)
+        vc8 = (g.kv_cache[:, 1].float() / vs).to(torch.float8_e4m3fn)
+
+        def step():  # noqa: F811
+            unified_attention_optimized(g.q, kc8, vc8, out, g.block_table, g.seqused_k, g.cu_seqlens_q, g.max_seqlen_q,
+                                        g.max_seqlen_k, g.softmax_scale, causal=True, num_splits_override=splits or None,
+                                        kv_quant_mode=1, k_descale=ks, v_descale=vs)
 
     for _ in range(max(warmup, 1)):
         step()
@@ -977,7 +994,7 @@ def attention_bench(args, world, rank, local):
 
     decode = args.workload.startswith("decode")
     r = attention_run(args.workload, args.splits, args.steps, args.warmup, world, rank, local, args.num_seqs,
-                      graph=args.graph)
+                      graph=args.graph, kv_quant=args.kv_quant)
     batch, out, stream = r["batch"], r["out"], r["stream"]
     max_ms, total_flops, total_tokens = r["max_ms"], r["total_flops"], r["total_tokens"]
 
@@ -991,7 +1008,8 @@ def attention_bench(args, world, rank, local):
         verify = verify_sharded(args.workload, args.num_seqs, batch, out, world, rank, args.splits)
 
     subs = None
-    if args.workload == "chunked_prefill_16k" and not args.no_sub and not args.num_seqs and HEAD_DIM == 128:
+    if (args.workload == "chunked_prefill_16k" and not args.no_sub and not args.num_seqs and HEAD_DIM == 128
+            and args.kv_quant == "none"):
         del r["g"], r["out"]
         out = None
         torch.cuda.empty_cache()
@@ -1016,6 +1034,8 @@ def attention_bench(args, world, rank, local):
             cpu = {"value": flops_s / statistics.mean(ts) / 1e12, "unit": "TFLOP/s",
                    "cores": torch.get_num_threads(), "kind": "port", "sample": desc}
     config = attention_config(args.workload, world, args.splits, args.num_seqs)
+    if args.kv_quant != "none":
+        config["kv_cache"] = f"{args.kv_quant} per-tensor (pages dequantised each call)"
     line = {
         "metric": METRIC,
         "value": r["value"],

@@ -896,9 +896,16 @@ int b200_kv_dequant_pages(const B200KvDequantParams* p, void* stream) {
   a.out = p->out_cache; a.out_table = p->out_block_table;
   a.num_seqs = p->num_seqs; a.max_pages = p->max_pages; a.block_size = p->block_size; a.hkv = p->num_kv_heads;
   a.head_dim = p->head_dim; a.num_blocks = p->num_blocks;
-  const dim3 grid((unsigned)p->max_pages, (unsigned)p->num_seqs);
+  const int64_t pages = (int64_t)p->max_pages * p->num_seqs;
+  const dim3 grid((unsigned)std::max<int64_t>(1, std::min<int64_t>(pages, (int64_t)sm_count() * 8)));
+  const bool vec8 = p->head_dim % 8 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(p->key_cache) | reinterpret_cast<uintptr_t>(p->value_cache)) & 7) == 0 &&
+                    ((p->kc_stride_block | p->kc_stride_tok | p->kc_stride_head | p->vc_stride_block |
+                      p->vc_stride_tok | p->vc_stride_head) & 7) == 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define B200_DQ(T, ELEM, PTH) b200::kv_dequant_kernel<T, ELEM, PTH><<<grid, b200::kDequantThreads, 0, s>>>(a);
+#define B200_DQ(T, ELEM, PTH)                                                                         \
+  if (vec8) b200::kv_dequant_kernel<T, ELEM, PTH, 8><<<grid, b200::kDequantThreads, 0, s>>>(a);       \
+  else b200::kv_dequant_kernel<T, ELEM, PTH, 4><<<grid, b200::kDequantThreads, 0, s>>>(a);
 #define B200_DQ_T(T)                                                                               \
   if (p->quant_mode == B200_KVQ_FP8_PER_TENSOR) {                                                  \
     if (p->cache_dtype == B200_DTYPE_FP8_E4M3) { B200_DQ(T, b200::kElemE4M3, false) }             \

@@ -18,9 +18,11 @@
 // table gets that index; pages past a sequence's length get a table entry and
 // no data.  A block id outside [0, num_blocks) gives a zero page.
 //
-// Bandwidth kernel: one CTA per (page, sequence), 4-byte loads (the
-// per-token-head rows carry their 4-byte scale inline, so rows are only
-// 4-byte aligned) and 8-byte stores.
+// Bandwidth kernel: a persistent grid-stride loop over the dense pages; 8-byte
+// loads and 16-byte stores when every cache row is 8-byte aligned, else 4-byte
+// loads and 8-byte stores (the per-token-head rows carry their 4-byte scale
+// inline, so they are only 4-byte aligned); four pieces per thread in flight
+// before any is stored.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -84,45 +86,82 @@ __device__ __forceinline__ uint2 encode4(const float (&f)[4]) {
   return r;
 }
 
-template <typename T, int kElem, bool kPerTokenHead>
+// A page: 2 (K, V) x block_size x hkv rows of head_dim elements, cut into
+// pieces of kPiece elements (8 when every cache row is 8-byte aligned, else 4),
+// consecutive threads on consecutive pieces, so a warp reads 128-256 and
+// writes 256-512 contiguous bytes per instruction.  Persistent grid-stride loop over the dense pages; every thread loads
+// its pieces of a page before converting and storing them.
+template <typename T, int kElem, bool kPerTokenHead, int kPiece>
 __global__ void __launch_bounds__(kDequantThreads) kv_dequant_kernel(const KvDequantArgs a) {
-  const int p = blockIdx.x, b = blockIdx.y;
-  const int dst_page = b * a.max_pages + p;
-  if (threadIdx.x == 0) a.out_table[dst_page] = dst_page;
-  const int L = static_cast<int>(kv_load_index(a.seqused, b, a.len_i64));
-  if (p * a.block_size >= L || p >= a.bt_cols) return;
-  const int64_t src = kv_load_index(a.block_table, static_cast<int64_t>(b) * a.bt_stride + p, a.bt_i64);
-  const bool have = src >= 0 && src < a.num_blocks;
-  const int q4 = a.head_dim / 4;  // 4-element pieces per row
-  const int per_cache = a.block_size * a.hkv * q4;
-  T* out = static_cast<T*>(a.out) + static_cast<int64_t>(dst_page) * 2 * a.block_size * a.hkv * a.head_dim;
+  constexpr int kPer = 4;  // pieces a thread keeps in flight per page
+  const int pieces_per_row = a.head_dim / kPiece;
+  const int per_cache = a.block_size * a.hkv * pieces_per_row;
+  const int total_pages = a.num_seqs * a.max_pages;
   const float ks_tensor = kPerTokenHead ? 1.f : __ldg(a.k_scale);
   const float vs_tensor = kPerTokenHead ? 1.f : __ldg(a.v_scale);
-  for (int i = threadIdx.x; i < 2 * per_cache; i += kDequantThreads) {
-    const int kv = i >= per_cache;
-    const int r = kv ? i - per_cache : i;
-    const int piece = r % q4;
-    const int row = r / q4;  // slot * hkv + head
-    const int slot = row / a.hkv, head = row - slot * a.hkv;
-    float f[4] = {0.f, 0.f, 0.f, 0.f};
-    if (have) {
-      const uint8_t* base = kv ? a.vc : a.kc;
-      const int64_t off = src * (kv ? a.vc_sb : a.kc_sb) + slot * (kv ? a.vc_st : a.kc_st) +
-                          head * (kv ? a.vc_sh : a.kc_sh) + 4 * piece;
-      decode4<kElem>(__ldg(reinterpret_cast<const uint32_t*>(base + off)), f);
-      float s;
-      if (kPerTokenHead) {
-        s = kv ? __ldg(a.vsc + src * a.vs_sb + slot * a.vs_st + head * a.vs_sh)
-               : __ldg(a.ksc + src * a.ks_sb + slot * a.ks_st + head * a.ks_sh);
-      } else {
-        s = kv ? vs_tensor : ks_tensor;
+  for (int dst_page = blockIdx.x; dst_page < total_pages; dst_page += gridDim.x) {
+    const int b = dst_page / a.max_pages, p = dst_page - b * a.max_pages;
+    if (threadIdx.x == 0) a.out_table[dst_page] = dst_page;
+    const int L = static_cast<int>(kv_load_index(a.seqused, b, a.len_i64));
+    if (p * a.block_size >= L || p >= a.bt_cols) continue;  // CTA-uniform
+    const int64_t src = kv_load_index(a.block_table, static_cast<int64_t>(b) * a.bt_stride + p, a.bt_i64);
+    const bool have = src >= 0 && src < a.num_blocks;
+    T* out = static_cast<T*>(a.out) + static_cast<int64_t>(dst_page) * 2 * a.block_size * a.hkv * a.head_dim;
+    for (int base = threadIdx.x; base < 2 * per_cache; base += kPer * kDequantThreads) {
+      uint32_t w[kPer][kPiece / 4];
+      float sc[kPer];
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int i = base + k * kDequantThreads;
+        sc[k] = 0.f;
+#pragma unroll
+        for (int e = 0; e < kPiece / 4; ++e) w[k][e] = 0u;
+        if (i < 2 * per_cache && have) {
+          const int kv = i >= per_cache;
+          const int r = kv ? i - per_cache : i;
+          const int piece = r % pieces_per_row, row = r / pieces_per_row;
+          const int slot = row / a.hkv, head = row - slot * a.hkv;
+          const uint8_t* src_row = (kv ? a.vc : a.kc) + src * (kv ? a.vc_sb : a.kc_sb) +
+                                   slot * (kv ? a.vc_st : a.kc_st) + head * (kv ? a.vc_sh : a.kc_sh);
+          if (kPiece == 8) {
+            const uint2 v = __ldg(reinterpret_cast<const uint2*>(src_row + 8 * piece));
+            w[k][0] = v.x; w[k][1] = v.y;
+          } else {
+            w[k][0] = __ldg(reinterpret_cast<const uint32_t*>(src_row + 4 * piece));
+          }
+          if (kPerTokenHead) {
+            sc[k] = kv ? __ldg(a.vsc + src * a.vs_sb + slot * a.vs_st + head * a.vs_sh)
+                       : __ldg(a.ksc + src * a.ks_sb + slot * a.ks_st + head * a.ks_sh);
+          } else {
+            sc[k] = kv ? vs_tensor : ks_tensor;
+          }
+        }
       }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) f[e] *= s;
+      for (int k = 0; k < kPer; ++k) {
+        const int i = base + k * kDequantThreads;
+        if (i >= 2 * per_cache) break;
+        const int kv = i >= per_cache;
+        const int r = kv ? i - per_cache : i;
+        const int piece = r % pieces_per_row, row = r / pieces_per_row;
+        // dense page layout [2][block_size][hkv][head_dim]
+        T* dst = out + (static_cast<int64_t>(kv) * a.block_size * a.hkv + row) * a.head_dim + kPiece * piece;
+        uint2 enc[kPiece / 4];
+#pragma unroll
+        for (int e = 0; e < kPiece / 4; ++e) {
+          float f[4];
+          decode4<kElem>(w[k][e], f);
+#pragma unroll
+          for (int x = 0; x < 4; ++x) f[x] *= sc[k];
+          enc[e] = encode4<T>(f);
+        }
+        if (kPiece == 8) {
+          *reinterpret_cast<uint4*>(dst) = make_uint4(enc[0].x, enc[0].y, enc[kPiece / 4 - 1].x, enc[kPiece / 4 - 1].y);
+        } else {
+          *reinterpret_cast<uint2*>(dst) = enc[0];
+        }
+      }
     }
-    // dense page layout [2][block_size][hkv][head_dim]
-    *reinterpret_cast<uint2*>(out + (static_cast<int64_t>(kv) * a.block_size * a.hkv + row) * a.head_dim +
-                              4 * piece) = encode4<T>(f);
   }
 }
 

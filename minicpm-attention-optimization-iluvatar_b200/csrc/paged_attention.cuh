@@ -1116,7 +1116,11 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
     qs[j] = n;
     my_tiles += static_cast<unsigned long long>(n);
   }
-  if (a.num_splits > 1) atomicAdd(&s_total_tiles, my_tiles);
+  if (a.num_splits > 1) {  // one shared atomic per warp (1024 on one word serialise)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) my_tiles += __shfl_xor_sync(0xffffffffu, my_tiles, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&s_total_tiles, my_tiles);
+  }
   __syncthreads();
   const long long total_tiles = static_cast<long long>(s_total_tiles) * a.num_kv_heads;
 

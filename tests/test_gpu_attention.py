@@ -361,7 +361,7 @@ def test_head_dim_64_decode_batch_and_dispatcher(monkeypatch):
     _no_device_error()
 
 
-@pytest.mark.parametrize("hq,hkv", [(16, 2), (8, 8), (16, 1), (12, 2)])
+@pytest.mark.parametrize("hq,hkv", [(16, 2), (8, 8), (16, 1), (12, 2), (32, 16)])
 def test_head_dim_256_against_oracle(hq, hkv):
     """head_dim 256 (accepted by the reference wrapper,
     kernels/triton_split_kv_paged.py:270): the kernel's wide variant, one
@@ -398,4 +398,21 @@ def test_head_dim_256_chunked_prefill_and_dispatcher(monkeypatch):
                        b.softmax_scale, causal=True, block_table=b.block_table)
     torch.cuda.synchronize()
     assert_close(out.cpu(), oracle(small_batch([20, 33], [100, 400], seed=259, head_dim=256)), "d256 dispatcher")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("head_dim", [64, 256])
+def test_head_sizes_with_page_size_32_int64_and_a_wide_table(head_dim):
+    """head_dim 64 and 256 with 32-token pages (two 16-key slices per page),
+    int64 block table and lengths, and a block table wider than needed."""
+    batch = small_batch([33, 7, 150], [100, 500, 1300], seed=head_dim + 5, block_size=32, extra_table_cols=5,
+                        head_dim=head_dim)
+    want = oracle(batch)
+    b = batch.to("cuda")
+    for s in (1, 4):
+        out = torch.empty_like(b.q)
+        paged_split_kv_attention(b.q, b.kv_cache[:, 0], b.kv_cache[:, 1], out, b.block_table.long(), b.seqused_k.long(),
+                                 b.cu_seqlens_q.long(), b.max_seqlen_q, b.max_seqlen_k, b.softmax_scale, num_splits=s)
+        torch.cuda.synchronize()
+        assert_close(out.cpu(), want, f"d{head_dim} bs32 int64 S={s}")
     _no_device_error()

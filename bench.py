@@ -132,14 +132,40 @@ def barrier(world):
         torch.cuda.synchronize()
 
 
+def _reduce_device():
+    """Where the small reductions run: the GPU under NCCL, the host under gloo."""
+    import torch.distributed as dist
+
+    return "cuda" if dist.get_backend() == "nccl" else "cpu"
+
+
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
     import torch.distributed as dist
 
-    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    t = torch.tensor([x], device=_reduce_device(), dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_over_ranks(x: float, world: int) -> list:
+    """Every rank's value of x, in rank order (a collective: all ranks call it)."""
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device=_reduce_device(), dtype=torch.float64)
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [float(p.item()) for p in parts]
+
+
+def rank_spread(rank_ms: list, steps: int) -> dict:
+    """Per-rank device time per call: the load balance of the sharding."""
+    per = [m / steps for m in rank_ms]
+    return {"min_ms": min(per), "max_ms": max(per), "max_over_min": max(per) / min(per),
+            "per_rank_ms": [round(x, 4) for x in per]}
 
 
 def sum_over_ranks(x: float, world: int) -> float:
@@ -147,7 +173,7 @@ def sum_over_ranks(x: float, world: int) -> float:
         return x
     import torch.distributed as dist
 
-    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    t = torch.tensor([x], device=_reduce_device(), dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
 
@@ -893,11 +919,12 @@ def attention_run(workload: str, splits: int, steps: int, warmup: int, world: in
     else:
         per_launch = [s.elapsed_time(e) for s, e in evs]
     max_ms = max_over_ranks(elapsed_ms, world)
+    rank_ms = gather_over_ranks(elapsed_ms, world)
     return {
         "batch": batch, "g": g, "out": out, "stream": stream, "resolved": resolved,
         "local_flops": local_flops, "local_bytes": local_bytes, "total_flops": total_flops,
         "total_bytes": total_bytes, "total_tokens": sum(all_q), "all_q": all_q,
-        "max_ms": max_ms, "per_launch": per_launch, "launch_ms": statistics.mean(per_launch),
+        "max_ms": max_ms, "rank_ms": rank_ms, "per_launch": per_launch, "launch_ms": statistics.mean(per_launch),
         "value": total_flops * steps / (max_ms * 1e-3) / 1e12,
         "tokens_per_s": sum(all_q) * steps / (max_ms * 1e-3),
         "clocks": sampler.summary() if sampler else None,
@@ -958,6 +985,8 @@ def sub_benchmarks(args, world, rank, local) -> dict:
                              "traffic": traffic_per_launch(workload) if splits == 0 else None,
                              "peak_kind": f"bf16_tflops (burst) of {kind}", "per_launch_ms": r["launch_ms"]},
             }
+            if world > 1:
+                subs[name]["rank_spread"] = rank_spread(r["rank_ms"], steps)
             if verify:
                 subs[name]["verify"] = verify
             del r
@@ -1064,6 +1093,7 @@ def attention_bench(args, world, rank, local):
     }
     if world > 1:
         line["rank0_ms_per_step"] = sum(r["per_launch"]) / args.steps
+        line["rank_spread"] = rank_spread(r["rank_ms"], args.steps)
     if verify:
         line["verify"] = verify
     if decode:

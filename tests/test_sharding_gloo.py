@@ -94,9 +94,15 @@ def _worker(rank, world, port, mode, result_q):
         padded = torch.full((6,), -1, dtype=torch.int64)
         padded[: len(ids)] = ids_t
         dist.all_gather(all_ids, padded)
+        # The bench's cross-rank reductions of a per-rank time (a collective
+        # each, in the same order on every rank).
+        import bench
+
+        x = 10.0 + 5.0 * rank
+        red = (bench.max_over_ranks(x, world), bench.sum_over_ranks(x, world), bench.gather_over_ranks(x, world))
         if rank == 0:
             order = [int(i) for t in all_ids for i in t.tolist() if i >= 0]
-            result_q.put(("ok", order, gathered.numpy().copy()))
+            result_q.put(("ok", order, gathered.numpy().copy(), red))
         dist.destroy_process_group()
     except SystemExit:
         raise
@@ -136,7 +142,12 @@ def _spawn(mode):
 def test_gloo_two_ranks_gather_matches_single_process():
     procs, results = _spawn("ok")
     assert all(p.exitcode == 0 for p in procs), [r for r in results if r[0] == "error"]
-    (_, order, gathered), = [r for r in results if r[0] == "ok"]
+    (_, order, gathered, red), = [r for r in results if r[0] == "ok"]
+    assert red == (15.0, 25.0, [10.0, 15.0])
+    import bench
+
+    spread = bench.rank_spread(red[2], 5)
+    assert spread["min_ms"] == 2.0 and spread["max_ms"] == 3.0 and spread["max_over_min"] == 1.5
     from oracle import paged_attention_reference
 
     q = [40, 1, 17, 1, 90, 3]

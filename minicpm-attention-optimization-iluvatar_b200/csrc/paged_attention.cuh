@@ -994,6 +994,47 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& 
   return before;
 }
 
+// Two exclusive prefix sums over the block in one pass (warp_sums: 64 ints).
+__device__ __forceinline__ void block_exclusive_scan2(int v0, int v1, int* warp_sums, int& before0, int& before1,
+                                                      int& total0, int& total1) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x0 = v0, x1 = v1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y0 = __shfl_up_sync(0xffffffffu, x0, o);
+    const int y1 = __shfl_up_sync(0xffffffffu, x1, o);
+    if (lane >= o) {
+      x0 += y0;
+      x1 += y1;
+    }
+  }
+  if (lane == 31) {
+    warp_sums[warp] = x0;
+    warp_sums[32 + warp] = x1;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int w0 = warp_sums[lane], w1 = warp_sums[32 + lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y0 = __shfl_up_sync(0xffffffffu, w0, o);
+      const int y1 = __shfl_up_sync(0xffffffffu, w1, o);
+      if (lane >= o) {
+        w0 += y0;
+        w1 += y1;
+      }
+    }
+    warp_sums[lane] = w0;  // inclusive over warps
+    warp_sums[32 + lane] = w1;
+  }
+  __syncthreads();
+  before0 = (warp > 0 ? warp_sums[warp - 1] : 0) + x0 - v0;
+  before1 = (warp > 0 ? warp_sums[32 + warp - 1] : 0) + x1 - v1;
+  total0 = warp_sums[31];
+  total1 = warp_sums[63];
+  __syncthreads();
+}
+
 // hist[i] := number of entries in buckets above i (exclusive prefix from the
 // top bucket down).
 __device__ __forceinline__ void buckets_to_offsets_desc(int* hist, int* warp_sums) {
@@ -1040,26 +1081,30 @@ __device__ __forceinline__ int qunit_splits(const SchedArgs& a, int n, long long
   return (n + tps - 1) / tps;                                             // no split left empty
 }
 
-// Dynamic shared memory of the schedule kernel: the per-sequence arrays
-// (query-unit prefix, query length, KV length) for up to kSchedSeqCache
-// sequences and the per-query-unit arrays (splits, work-unit prefix, split
-// slot) for up to kSchedQunitCache query units; larger batches keep them in
-// the workspace.  Every pass then reads shared memory, and global memory is
-// read once per value.
+// Dynamic shared memory of the schedule kernel: the schedule's tail (its
+// last kSchedThreads units, re-sorted at the end), the per-sequence arrays
+// (query-unit prefix, query length, KV length, first work-list slot) for up
+// to kSchedSeqCache sequences and the per-query-unit arrays (splits,
+// work-unit prefix, split slot, sequence) for up to kSchedQunitCache query units;
+// larger batches keep them in the workspace.  Every pass then reads shared
+// memory, and global memory is read once per value.
 constexpr int kSchedQunitCache = 8192;
 constexpr uint32_t kSchedSmemBytes =
-    4 * (kSchedBuckets + 32 + 3 * kSchedSeqCache + 1 + 3 * kSchedQunitCache + 1);
+    16 * kSchedThreads + 4 * (kSchedBuckets + 64 + 4 * kSchedSeqCache + 1 + 4 * kSchedQunitCache + 1);
 
 __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const SchedArgs a) {
-  extern __shared__ int sched_smem[];
-  int* hist = sched_smem;                                // [kSchedBuckets]
-  int* warp_sums = hist + kSchedBuckets;                 // [32]
-  int* s_tb = warp_sums + 32;                            // [kSchedSeqCache + 1]
+  extern __shared__ int4 sched_smem[];
+  int4* s_tail = sched_smem;                             // [kSchedThreads]
+  int* hist = reinterpret_cast<int*>(s_tail + kSchedThreads);  // [kSchedBuckets]
+  int* warp_sums = hist + kSchedBuckets;                 // [64]
+  int* s_tb = warp_sums + 64;                            // [kSchedSeqCache + 1]
   int* s_ql = s_tb + kSchedSeqCache + 1;                 // [kSchedSeqCache]
   int* s_L = s_ql + kSchedSeqCache;                      // [kSchedSeqCache]
-  int* s_qs = s_L + kSchedSeqCache;                      // [kSchedQunitCache]
+  int* s_so = s_L + kSchedSeqCache;                      // [kSchedSeqCache]
+  int* s_qs = s_so + kSchedSeqCache;                     // [kSchedQunitCache]
   int* s_qb = s_qs + kSchedQunitCache;                   // [kSchedQunitCache + 1]
   int* s_qslot = s_qb + kSchedQunitCache + 1;            // [kSchedQunitCache]
+  int* s_qseq = s_qslot + kSchedQunitCache;              // [kSchedQunitCache]
   __shared__ int s_total_qunits;
   __shared__ unsigned long long s_total_tiles;
   griddep_launch_dependents();  // the attention grid may launch; it waits for this one
@@ -1107,13 +1152,21 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   int* qb = q_cached ? s_qb : a.qunit_base;
   int* qslot = q_cached ? s_qslot : a.qunit_slot;
 
+  // Each thread takes a contiguous run of query units: one search for the
+  // run's first sequence, then a walk along the runs in every pass.
+  const int q_per = (nq + kSchedThreads - 1) / kSchedThreads;
+  const int j_begin = min(static_cast<int>(threadIdx.x) * q_per, nq);
+  const int j_end = min(j_begin + q_per, nq);
+  const int seq_begin = j_begin < nq ? upper_index(tb, a.num_seqs, j_begin) : 0;
+
   // 2. KV tiles of each query unit's whole key range (kept in qs for now) and
   // their sum over query units and KV heads.
   unsigned long long my_tiles = 0;
-  for (int j = threadIdx.x; j < nq; j += kSchedThreads) {
-    const int seq = upper_index(tb, a.num_seqs, j);
+  for (int j = j_begin, seq = seq_begin; j < j_end; ++j) {
+    while (tb[seq + 1] <= j) ++seq;  // past empty sequences
     const int n = qunit_full_tiles(q_len(seq), kv_len(seq), j - tb[seq], a.pos_per_unit);
     qs[j] = n;
+    if (q_cached) s_qseq[j] = seq;
     my_tiles += static_cast<unsigned long long>(n);
   }
   if (a.num_splits > 1) {  // one shared atomic per warp (1024 on one word serialise)
@@ -1124,23 +1177,23 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   __syncthreads();
   const long long total_tiles = static_cast<long long>(s_total_tiles) * a.num_kv_heads;
 
-  // 3. splits per query unit; work units and split slots, exclusive prefixes.
-  int ucarry = 0, scarry = 0;
-  for (int base = 0; base < nq; base += kSchedThreads) {
-    const int j = base + threadIdx.x;
-    int s = 1;
-    if (j < nq) s = qunit_splits(a, qs[j], total_tiles);
-    int utotal, stotal = 0;
-    const int ubefore = block_exclusive_scan(j < nq ? s * a.num_kv_heads : 0, warp_sums, utotal);
-    int sbefore = 0;
-    if (a.num_splits > 1) sbefore = block_exclusive_scan(j < nq && s > 1 ? 1 : 0, warp_sums, stotal);
-    if (j < nq) {
-      qs[j] = s;
-      qb[j] = ucarry + ubefore;
-      qslot[j] = s > 1 ? scarry + sbefore : -1;
-    }
-    ucarry += utotal;
-    scarry += stotal;
+  // 3. splits per query unit; work units and split slots, exclusive prefixes
+  // (one block scan over the runs' sums).
+  int my_units = 0, my_split = 0;
+  for (int j = j_begin; j < j_end; ++j) {
+    const int sp = qunit_splits(a, qs[j], total_tiles);
+    qs[j] = sp;
+    my_units += sp * a.num_kv_heads;
+    my_split += sp > 1 ? 1 : 0;
+  }
+  int ubefore, sbefore, ucarry, scarry;
+  block_exclusive_scan2(my_units, my_split, warp_sums, ubefore, sbefore, ucarry, scarry);
+  for (int j = j_begin; j < j_end; ++j) {
+    const int sp = qs[j];
+    qb[j] = ubefore;
+    qslot[j] = sp > 1 ? sbefore : -1;
+    ubefore += sp * a.num_kv_heads;
+    sbefore += sp > 1 ? 1 : 0;
   }
   if (threadIdx.x == 0) qb[nq] = ucarry;
   __syncthreads();
@@ -1162,37 +1215,48 @@ __global__ void __launch_bounds__(kSchedThreads, 1) attn_schedule_kernel(const S
   __syncthreads();
   for (int b = threadIdx.x; b < a.num_seqs; b += kSchedThreads) {
     const int qt = tb[b + 1] - tb[b];
-    if (qt > 0) a.seq_off[b] = atomicAdd(&hist[seq_bucket_of(b, qt)], seq_units(b));
+    if (qt > 0) {
+      const int off = atomicAdd(&hist[seq_bucket_of(b, qt)], seq_units(b));
+      a.seq_off[b] = off;
+      if (seq_cached) s_so[b] = off;
+    }
   }
   __syncthreads();
-  // 5. scatter, one query unit per thread: its units (KV head, then split)
-  // go to its sequence's range, the sequence's last query unit first.
+  const int* so = seq_cached ? s_so : a.seq_off;
+  // 5. scatter, one query unit per thread (adjacent threads write adjacent
+  // units): a query unit's units (KV head, then split) go to its sequence's
+  // range, the sequence's last query unit first.  The units that land in the
+  // schedule's tail are also kept in shared memory for step 6.
+  const int tail = min(total_units, kSchedThreads);
+  const int tail0 = total_units - tail;
   for (int j = threadIdx.x; j < nq; j += kSchedThreads) {
-    const int seq = upper_index(tb, a.num_seqs, j);
-    const int s = qs[j];
+    const int seq = q_cached ? s_qseq[j] : upper_index(tb, a.num_seqs, j);
+    const int sp = qs[j];
     const int first = qb[j];
     const int qunit = j - tb[seq];
-    const int pos0 = a.seq_off[seq] + (qb[tb[seq + 1]] - qb[j + 1]);
-    const int slot0 = s > 1 ? qslot[j] * a.num_kv_heads : -1;
-    for (int rem = 0; rem < s * a.num_kv_heads && first + rem < total_units; ++rem) {
-      const int kvh = rem / s;
-      const int split = rem - kvh * s;
-      const int slot = s > 1 ? slot0 + kvh : -1;
-      if (pos0 + rem < a.capacity) a.units[pos0 + rem] = pack_unit(seq, qunit, kvh, split, s, slot);
-      if (s > 1 && split == 0) a.split_units[slot] = make_int4(seq, qunit, kvh, s);
+    const int pos0 = so[seq] + (qb[tb[seq + 1]] - qb[j + 1]);
+    const int slot0 = sp > 1 ? qslot[j] * a.num_kv_heads : -1;
+    for (int rem = 0; rem < sp * a.num_kv_heads && first + rem < total_units; ++rem) {
+      const int kvh = rem / sp;
+      const int split = rem - kvh * sp;
+      const int slot = sp > 1 ? slot0 + kvh : -1;
+      const int pos = pos0 + rem;
+      const int4 u = pack_unit(seq, qunit, kvh, split, sp, slot);
+      if (pos < a.capacity) a.units[pos] = u;
+      if (pos >= tail0 && pos < total_units) s_tail[pos - tail0] = u;
+      if (sp > 1 && split == 0) a.split_units[slot] = make_int4(seq, qunit, kvh, sp);
     }
   }
   __syncthreads();
   // 6. the schedule's tail, its last kSchedThreads units, by KV-tile count
   // across sequences, heaviest first, so the last units claimed are the
   // smallest.
-  const int tail = min(total_units, kSchedThreads);
-  const int tail0 = total_units - tail;
   const bool mine = static_cast<int>(threadIdx.x) < tail;
   int4 unit = make_int4(0, 0, 0, 0);
   int bucket = 0;
   if (mine) {
-    unit = a.units[tail0 + threadIdx.x];
+    // Every tail slot was written in step 5 unless the capacity clipped the list.
+    unit = ucarry == total_units ? s_tail[threadIdx.x] : a.units[tail0 + threadIdx.x];
     int kvh, split, nsplit;
     unpack_unit(unit, kvh, split, nsplit);
     const int q0 = seq_cached ? 0 : load_index(a.cu_q, unit.x, a.len_i64);

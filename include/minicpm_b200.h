@@ -358,6 +358,15 @@ B200_API const char* b200_last_error(void);
  */
 B200_API int b200_device_error(void* stream, uint32_t* code);
 
+/*
+ * Test hook for the bounded waits (no reference counterpart): launches one
+ * warp on `stream` that waits on an mbarrier nothing ever arrives on.  The
+ * wait gives up after its limit (2 s of %globaltimer), records
+ * B200_DEVERR_WAIT_TIMEOUT and the kernel returns, so the context stays
+ * usable; b200_device_error then reports the timeout.  Never faults or hangs.
+ */
+B200_API int b200_wait_selftest(void* stream);
+
 B200_API int b200_abi_version(void);
 
 #ifdef __cplusplus

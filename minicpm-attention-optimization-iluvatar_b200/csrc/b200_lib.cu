@@ -27,6 +27,26 @@
 #include "kv_cache_write.cuh"
 #include "kv_dequant.cuh"
 
+namespace b200 {
+
+// b200_wait_selftest: one warp waits on an mbarrier that nothing arrives on.
+// The bounded wait (mbar_wait) gives up after B200_WAIT_LIMIT_NS, records
+// B200_DEVERR_WAIT_TIMEOUT and raises the abort flag; the kernel then returns.
+__global__ void __launch_bounds__(32, 1) wait_selftest_kernel() {
+  __shared__ __align__(8) uint64_t bar_word;
+  __shared__ int abort_word;
+  const uint32_t bar = smem_addr(&bar_word);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    abort_word = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  mbar_wait(bar, 0, &abort_word);
+}
+
+}  // namespace b200
+
 namespace {
 
 thread_local char g_last_error[512] = "";
@@ -916,6 +936,11 @@ int b200_kv_dequant_pages(const B200KvDequantParams* p, void* stream) {
 #undef B200_DQ_T
 #undef B200_DQ
   return check_launch("kv_dequant_kernel");
+}
+
+int b200_wait_selftest(void* stream) {
+  b200::wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+  return check_launch("wait_selftest_kernel");
 }
 
 int b200_device_error(void* stream, uint32_t* code) {

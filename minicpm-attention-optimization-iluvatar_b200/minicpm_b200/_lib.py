@@ -69,6 +69,7 @@ EXPORTED_SYMBOLS = (
     "b200_kv_cache_write",
     "b200_kv_dequant_pages",
     "b200_device_error",
+    "b200_wait_selftest",
 )
 
 c_void_p = ctypes.c_void_p
@@ -195,6 +196,8 @@ def load() -> ctypes.CDLL:
         lib.b200_kv_dequant_pages.argtypes = [ctypes.POINTER(KvDequantParams), c_void_p]
         lib.b200_device_error.restype = ctypes.c_int
         lib.b200_device_error.argtypes = [c_void_p, ctypes.POINTER(ctypes.c_uint32)]
+        lib.b200_wait_selftest.restype = ctypes.c_int
+        lib.b200_wait_selftest.argtypes = [c_void_p]
         if lib.b200_abi_version() != ABI_VERSION:
             raise RuntimeError("libminicpm_b200.so ABI version mismatch; rebuild it")
         _lib = lib

@@ -70,6 +70,8 @@ def test_invalid_params_return_status_not_crash():
     assert lib.b200_rope_kv_write(ctypes.byref(r), None) == _lib.B200_ERR_INVALID
     c = _lib.CombineParams(num_splits=17, num_heads=16, head_dim=128)
     assert lib.b200_split_combine(ctypes.byref(c), None) == _lib.B200_ERR_INVALID
+    if not torch.cuda.is_available():  # the launch itself fails with a status, not a crash
+        assert lib.b200_wait_selftest(None) == _lib.B200_ERR_CUDA
 
 
 def _attn_args(**over):

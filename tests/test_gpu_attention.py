@@ -191,6 +191,27 @@ def _split_slots() -> int:
     return int(ws[:12].cpu().view(torch.int32)[2])
 
 
+def test_schedule_beyond_its_shared_memory_caches(monkeypatch):
+    """9000 sequences and 9015 query units: more than the schedule kernel keeps
+    in shared memory (4096 sequences, 8192 query units), so every pass reads
+    the workspace arrays instead; two long sequences among the short ones.
+    Sampled sequences against the oracle at S = auto / 4 and every unit split
+    4 ways."""
+    n = 9000
+    q = [2] * n
+    kv = [40 + (i % 7) * 9 for i in range(n)]
+    q[5], kv[5] = 300, 5000
+    q[4000], kv[4000] = 200, 3000
+    batch = build_attention_batch(q, kv, seed=9000)
+    picks = [(s, 0, q[s]) for s in range(0, n, 97)] + [(5, 0, 300), (4000, 0, 200), (n - 1, 0, 2)]
+    want, rows = sampled_oracle(batch, picks)
+    for s in (0, 4):
+        assert_close(run_gpu(batch, s)[rows], want, f"9000 seqs S={s}")
+    monkeypatch.setenv("B200_ATTN_SPLIT_UNIFORM", "1")
+    assert_close(run_gpu(batch, 4)[rows], want, "9000 seqs uniform S=4")
+    _no_device_error()
+
+
 def test_split_policy_splits_small_batches_only():
     """num_splits is the most any query unit gets: the reference's third unit
     case (few sequences, long keys) is split, the 4K config (13 waves of units

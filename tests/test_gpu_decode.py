@@ -39,6 +39,23 @@ def test_edge_lengths():
     _no_device_error()
 
 
+def test_more_sequences_than_the_schedule_caches():
+    """5000 decode rows: past the decode schedule's shared-memory copy of the
+    item prefix (4096 sequences), so it searches the workspace array; every
+    97th row and the last ones against the oracle."""
+    n = 5000
+    kv = [1 + (i * 37) % 700 for i in range(n)]
+    kv[17] = 9000  # one long row among the short ones
+    batch = _decode_batch(kv, seed=5000)
+    got = run_gpu(batch, 0)
+    picks = list(range(0, n, 97)) + [17, n - 2, n - 1]
+    sub = build_attention_batch([1] * len(picks), [kv[i] for i in picks], seed=5000, seq_ids=picks)
+    # content is keyed on the sequence ids, so the sub-batch holds the same rows
+    assert torch.equal(sub.q, batch.q[picks])
+    assert_close(got[picks], oracle(sub), "5000 decode rows")
+    _no_device_error()
+
+
 def test_matches_prefill_kernel(monkeypatch):
     batch = _decode_batch([333, 4096, 70, 12000, 1, 640], seed=22)
     got = run_gpu(batch, 0)
